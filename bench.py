@@ -1,0 +1,544 @@
+#!/usr/bin/env python
+"""Benchmark of the SpikeStack Lite hot path on B200.
+
+Default workload (one "step"): the isolated spike-linear configuration --
+binary spikes S[T=3, M=16384, K=512] ~ Bernoulli(0.10) per plane, W[K=512,
+N=128] fp32 ~ N(0, 1/K), output Y fp32 [T, M, N], CSR built per plane --
+through the engine's spike-linear (dense tcgen05 branch + per-plane CSR).
+Metric: GSOP/s, SOP = one (nonzero input spike, output neuron) accumulate,
+SOPs per step = nnz(S) * N.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload spike_linear|sweep|attention|model_small|model_full]
+
+N > 1: launched by torchrun, one rank per GPU; every rank runs its own
+instance (the rows are independent -> weak scaling, no collective on the data
+path); value = all ranks' SOPs / max-over-ranks device time.
+--impl reference: the reference's own CPU implementation of the path (its
+torch.matmul fallback, restated in oracle/) timed on the host cores, rank 0
+only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "tokens/s full-model fwd & spike-linear GSOP/s (% HBM roofline) at 1/2/4/8 B200"
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ------------------------------------------------------------------ utilities
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded in profiles/<name>.md ('dram_bytes_per_launch: N')."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        time.sleep(0.2)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self, backend="nccl"):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local) if backend == "nccl" else None)
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device=torch.device("cuda", self.local))
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- spike-linear
+def spike_linear_setup(cfg, dev, nsets, seed):
+    T, M, K, N, p = cfg["T"], cfg["M"], cfg["K"], cfg["N"], cfg["p"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    wdt = torch.bfloat16 if cfg["w_dtype"] == "bf16" else torch.float32
+    W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).to(wdt)  # weightT layout [K, N]
+    sets = []
+    for i in range(nsets):
+        S = (torch.rand(T, M, K, generator=g, device=dev) < p).float()
+        nnz = int((S > 0).sum().item())
+        csr = None
+        if cfg["csr"]:
+            from spikestack_lite_b200 import ops
+
+            csr = ops.alloc_csr(T, M, K, dev, capacity=int(nnz * 1.02) + 1024)
+        sets.append({"S": S, "nnz": nnz, "csr": csr})
+    return W, sets
+
+
+def run_spike_linear(args, dist, cfg):
+    from spikestack_lite_b200 import _lib, ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    T, M, K, N = cfg["T"], cfg["M"], cfg["K"], cfg["N"]
+    set_bytes = 4 * T * M * K + 4 * T * M * N
+    nsets = max(2, int(np.ceil(3 * L2_BYTES / set_bytes)) + 1)
+    W, sets = spike_linear_setup(cfg, dev, nsets, seed=1234 + dist.rank)
+    branch = args.branch
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        s = sets[i % nsets]
+        return ops.spike_linear(s["S"], weightT=W, csr=s["csr"], branch=branch)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+
+    # CUDA graphs (one per input set) keep the host out of the timed region
+    graphs = []
+    outs = []
+    for i in range(nsets):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            outs.append(step(i))
+        graphs.append(gph)
+    for i in range(nsets):
+        graphs[i].replay()
+    torch.cuda.synchronize()
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            graphs[i % nsets].replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    ms_max = dist.max(ms)
+    launches_per_step = (_lib.launch_count() - launches0) / max(1, nsets)  # counted at capture
+
+    sops_step = statistics.mean(s["nnz"] for s in sets) * N
+    value = dist.world * sops_step * args.steps / (ms_max / 1e3) / 1e9
+
+    # per-kernel device time with CUDA events on the launch stream (eager steps)
+    kernel_ms = {}
+    for kname in ("dense", "csr_scan", "w_image", "spmm_csr"):
+        _lib.profile_begin(kname)
+        for i in range(args.steps):
+            step(i)
+        tot, n = _lib.profile_end()
+        if n:
+            kernel_ms[kname] = tot / n
+    torch.cuda.synchronize()
+
+    # parity spot check of the timed outputs (one set) against the oracle
+    from oracle import spk_oracle as O
+
+    ref = O.spike_linear(sets[0]["S"][:, :2048].cpu().numpy(), W.float().cpu().numpy())
+    parity = O.rel_err(outs[0][:, :2048].cpu().numpy(), ref)
+
+    # end to end through the public API from pinned host buffers
+    e2e = spike_linear_e2e(args, dist, cfg, W, sets, branch)
+
+    pk = peaks()
+    alg_dense = 4 * T * M * K + W.element_size() * K * N + 4 * T * M * N
+    alg_step = alg_dense + (4 * T * (M + 1) + 4 * T * M + 4 * statistics.mean(s["nnz"] for s in sets)
+                            if cfg["csr"] else 0)
+    dom = "dense" if kernel_ms.get("dense") else "spmm_csr"
+    dom_ms = kernel_ms.get(dom)
+    achieved = alg_dense / (dom_ms / 1e3) / 1e9 if dom_ms else None
+    step_ms = ms_max / args.steps
+    res = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GSOP/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if cfg["w_dtype"] == "f32" else "bf16", "data": "synthetic",
+        "config": {"workload": cfg["name"], "T": T, "M": M, "K": K, "N": N, "p": cfg["p"], "w_dtype": cfg["w_dtype"],
+                   "csr_per_plane": cfg["csr"], "branch": branch, "per_rank_rows": T * M,
+                   "l2": f"{nsets} rotating input sets ({nsets * set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+                   "timing": "CUDA graph per input set, CUDA events, max over ranks"},
+        "step_gbs": round(alg_step / (step_ms / 1e3) / 1e9, 1),
+        "step_hbm_frac": round(alg_step / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+        "kernel_ms": {k: round(v, 5) for k, v in kernel_ms.items()},
+        "roofline": {"kernel": "spike_linear_tc_kernel" if dom == "dense" else "spmm_csr_kernel", "bound": "hbm",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4) if achieved else None,
+                     "peak_src": pk["src"], "alg_bytes_per_launch": int(alg_dense),
+                     "traffic": profile_traffic("spike_linear_dense_c2")},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "parity_rel_err": parity,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_spike_linear(cfg, sets[0]["S"], W)
+    return res
+
+
+def spike_linear_e2e(args, dist, cfg, W, sets, branch):
+    """Same metric through ops.spike_linear from pinned host buffers: every step
+    copies its S in (H2D) and its Y and CSR out (D2H); copies and compute run on
+    separate streams, double-buffered."""
+    from spikestack_lite_b200 import ops
+
+    dev = W.device
+    T, M, K, N = cfg["T"], cfg["M"], cfg["K"], cfg["N"]
+    hosts = [s["S"].cpu().pin_memory() for s in sets[:2]]
+    dS = [torch.empty_like(sets[0]["S"]) for _ in range(2)]
+    cap = max(s["csr"]["col_idx"].numel() for s in sets) if cfg["csr"] else 0
+    csrs = [ops.alloc_csr(T, M, K, dev, capacity=cap) if cfg["csr"] else None for _ in range(2)]
+    hY = [torch.empty(T, M, N, dtype=torch.float32).pin_memory() for _ in range(2)]
+    hC = [torch.empty(cap, dtype=torch.int32).pin_memory() if cfg["csr"] else None for _ in range(2)]
+    hR = [torch.empty(T * (M + 1), dtype=torch.int32).pin_memory() if cfg["csr"] else None for _ in range(2)]
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.current_stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_cmp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    h2d = hosts[0].numel() * 4
+    d2h = T * M * N * 4 + ((cap + T * (M + 1)) * 4 if cfg["csr"] else 0)
+
+    def one(i, record=None):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_cmp[b])  # buffer b free (its previous compute done)
+            dS[b].copy_(hosts[b], non_blocking=True)
+            ev_in[b].record(s_in)
+        s_cmp.wait_event(ev_in[b])
+        s_cmp.wait_event(ev_out[b])  # previous readback of buffer b done
+        Y = ops.spike_linear(dS[b], weightT=W, csr=csrs[b], branch=branch)
+        ev_cmp[b].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_cmp[b])
+            hY[b].copy_(Y, non_blocking=True)
+            if csrs[b] is not None:
+                hC[b].copy_(csrs[b]["col_idx"][:cap], non_blocking=True)
+                hR[b].copy_(csrs[b]["row_ptr"], non_blocking=True)
+            Y.record_stream(s_out)
+            ev_out[b].record(s_out)
+
+    for i in range(max(2, args.warmup)):
+        one(i)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(3, args.steps // 2)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start.record(s_in)
+    for i in range(steps):
+        one(i)
+    stop.record(s_out)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(start.elapsed_time(stop))
+    nnz = statistics.mean(s["nnz"] for s in sets[:2])
+    return {"value": round(dist.world * nnz * N * steps / (ms / 1e3) / 1e9, 2), "unit": "GSOP/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(ms / steps, 4), "api": "spikestack_lite_b200.ops.spike_linear"}
+
+
+def cpu_baseline_spike_linear(cfg, S_dev, W, budget_s=10.0):
+    """The reference's CPU path (torch.matmul fallback, sparse/__init__.py:104-105,
+    restated in oracle/) on a bounded sample, all host threads."""
+    from oracle import spk_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    S = S_dev.cpu()
+    Wc = W.float().cpu()
+    nnz = float((S > 0).sum().item())
+    O.reference_cpu_step(S, Wc)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        O.reference_cpu_step(S, Wc)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(nnz * cfg["N"] / t / 1e9, 3), "unit": "GSOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"full step ({cfg['T']}x{cfg['M']}x{cfg['K']}), median of {len(times)} runs",
+            "ms_per_step": round(t * 1e3, 3)}
+
+
+def run_reference_spike_linear(args, dist, cfg):
+    """--impl reference: the reference's CPU implementation, rank 0 only."""
+    from oracle import spk_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1234)
+    T, M, K, N = cfg["T"], cfg["M"], cfg["K"], cfg["N"]
+    W = torch.randn(K, N, generator=g) / K ** 0.5
+    S = (torch.rand(T, M, K, generator=g) < cfg["p"]).float()
+    nnz = float((S > 0).sum().item())
+    for _ in range(args.warmup):
+        O.reference_cpu_step(S, W)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.reference_cpu_step(S, W)
+    dt = time.perf_counter() - t0
+    v = round(nnz * N * args.steps / dt / 1e9, 3)
+    return {"metric": METRIC, "value": v, "unit": "GSOP/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": cfg["name"], "T": T, "M": M, "K": K, "N": N, "p": cfg["p"],
+                       "w_dtype": cfg["w_dtype"]},
+            "cpu_baseline": {"value": v, "unit": "GSOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": "full step per iteration (reference CPU path: torch.matmul, no CSR)"},
+            "e2e": {"value": v, "unit": "GSOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------- attention
+def run_attention(args, dist, cfg):
+    from spikestack_lite_b200 import _lib, ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    TB, L, H, dh = cfg["T"] * cfg["B"], cfg["L"], cfg["H"], cfg["dh"]
+    g = torch.Generator(device=dev).manual_seed(7 + dist.rank)
+    q, k, v = ((torch.rand(TB, L, H * dh, generator=g, device=dev) < cfg["p"]).float() for _ in range(3))
+    lam = torch.sigmoid(torch.empty(H * dh, device=dev).uniform_(5.0, 8.0, generator=g))
+    for _ in range(args.warmup):
+        ops.spiking_attention(q, k, v, lam, H)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    start.record()
+    for _ in range(args.steps):
+        ops.spiking_attention(q, k, v, lam, H)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = dist.max(start.elapsed_time(stop)) / args.steps
+    kms = {}
+    for kn in ("attn_kv", "attn_out"):
+        _lib.profile_begin(kn)
+        for _ in range(max(3, args.steps // 4)):
+            ops.spiking_attention(q, k, v, lam, H)
+        tot, n = _lib.profile_end()
+        kms[kn] = tot / max(n, 1)
+    bytes_ = 4 * 4 * TB * L * H * dh
+    pk = peaks()
+    tokens = cfg["B"] * L
+    return {"metric": METRIC, "value": round(dist.world * tokens / (ms / 1e3), 1), "unit": "tokens/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], **{k_: cfg[k_] for k_ in ("T", "B", "L", "H", "dh", "p")}},
+            "kernel_ms": {k_: round(v_, 4) for k_, v_ in kms.items()},
+            "roofline": {"kernel": "attention (kv + out)", "bound": "hbm",
+                         "achieved": round(bytes_ / (ms / 1e3) / 1e9, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(bytes_ / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}}
+
+
+# ------------------------------------------------------------------- model
+def run_model(args, dist, cfg):
+    from spikestack_lite_b200.transformer import SpikingTransformer
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.manual_seed(0)
+    model = SpikingTransformer(**cfg["model"]).to(dev).eval()
+    B = cfg["batch"]
+    per = B // dist.world
+    g = torch.Generator().manual_seed(1)
+    x_all = torch.randn(B, cfg["model"]["seq_len"], cfg["model"]["input_dim"], generator=g)
+    x = x_all[dist.rank * per:(dist.rank + 1) * per].to(dev)
+    chunk = cfg.get("chunk", per)
+
+    def fwd():
+        outs = [model(x[i:i + chunk]) for i in range(0, per, chunk)]
+        logits = torch.cat(outs)
+        if dist.pg:
+            import torch.distributed as tdist
+
+            full = torch.empty(B, logits.shape[1], device=dev)
+            tdist.all_gather_into_tensor(full, logits.contiguous())
+            return full
+        return logits
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            fwd()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        start.record()
+        for _ in range(args.steps):
+            logits = fwd()
+        stop.record()
+        torch.cuda.synchronize()
+    ms = dist.max(start.elapsed_time(stop)) / args.steps
+    tokens = B * cfg["model"]["seq_len"]
+    return {"metric": METRIC, "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "global_batch": B, "seq_len": cfg["model"]["seq_len"],
+                       "parallelism": f"batch-sharded x{dist.world}, NCCL all_gather of logits"},
+            "logits_checksum": float(logits.double().sum().item())}
+
+
+WORKLOADS = {
+    "spike_linear": {"name": "isolated spike-linear S[3,16384,512] p=0.10, W[512,128] fp32, CSR per plane",
+                     "T": 3, "M": 16384, "K": 512, "N": 128, "p": 0.10, "w_dtype": "f32", "csr": True},
+    "sweep": {"name": "spike-linear density sweep S[4,65536,2048], W[2048,2048] bf16", "T": 4, "M": 65536,
+              "K": 2048, "N": 2048, "p": 0.10, "w_dtype": "bf16", "csr": False},
+    "attention": {"name": "spiking linear attention B=64 H=8 L=4096 dh=64 T=4 p=0.15", "T": 4, "B": 64,
+                  "L": 4096, "H": 8, "dh": 64, "p": 0.15},
+    "model_small": {"name": "SpikingTransformer fwd, batch 256, seq 64, d 128, 1 layer, T=3", "batch": 256,
+                    "model": dict(input_dim=48, d_model=128, seq_len=64, num_classes=10, num_heads=4, num_layers=1,
+                                  n_repeats=3, temporal=True, expansion=4, use_spikeskip=True)},
+    "model_full": {"name": "SpikingTransformer fwd, batch 512, seq 1024, d 512, 6 layers, T=4, GSMC", "batch": 512,
+                   "chunk": 64,
+                   "model": dict(input_dim=256, d_model=512, seq_len=1024, num_classes=10, num_heads=8,
+                                 num_layers=6, n_repeats=4, temporal=True, expansion=4, use_gsmc=True,
+                                 use_exact=True, use_spikeskip=True)},
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="spike_linear", choices=sorted(WORKLOADS))
+    ap.add_argument("--p", type=float, default=None, help="spike density override")
+    ap.add_argument("--branch", default="dense", choices=["auto", "dense", "csr"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = dict(WORKLOADS[args.workload])
+    if args.p is not None:
+        cfg["p"] = args.p
+    dist = Dist()
+
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return
+        if args.workload != "spike_linear":
+            print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the default "
+                              "workload only"}))
+            return
+        print(json.dumps(run_reference_spike_linear(args, dist, cfg)), flush=True)
+        return
+
+    dist.init("nccl")
+    try:
+        if args.workload in ("spike_linear", "sweep"):
+            res = run_spike_linear(args, dist, cfg)
+        elif args.workload == "attention":
+            res = run_attention(args, dist, cfg)
+        else:
+            res = run_model(args, dist, cfg)
+        if dist.rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,68 @@
+"""Build the reference's own CUDA engines from its sources, as a second checker.
+
+Compiles, from a checkout of Griffith-7/spikestack-lite (default
+/root/reference, read-only), the three engines on the hot path
+
+    spikestack_lite/sparse/src/sparse_linear.cu   -> oracle/_ref/spikeskip_ref/
+    spikestack_lite/nn/src/attention_cuda.cu      -> oracle/_ref/attention_ref/
+    spikestack_lite/nn/src/gsmc_cuda.cu           -> oracle/_ref/gsmc_ref/
+
+as PyTorch extensions for sm_100a with torch.utils.cpp_extension (not the
+reference's own setup.py).  Outputs go only to oracle/_ref/ (git-ignored; the
+built .so files travel to the GPU box with the working tree, the sources do
+not).  TEST INFRASTRUCTURE ONLY: tests load these modules to compare against
+the reference engine on the GPU; the product never touches them.
+"""
+import argparse
+import importlib.machinery
+import importlib.util
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "_ref")
+ENGINES = {
+    "spikeskip_ref": "spikestack_lite/sparse/src/sparse_linear.cu",
+    "attention_ref": "spikestack_lite/nn/src/attention_cuda.cu",
+    "gsmc_ref": "spikestack_lite/nn/src/gsmc_cuda.cu",
+}
+
+
+def build_ref(reference="/root/reference", verbose=False):
+    from torch.utils.cpp_extension import load
+
+    built = {}
+    for name, rel in ENGINES.items():
+        src = os.path.join(reference, rel)
+        if not os.path.exists(src):
+            continue
+        bdir = os.path.join(REF_DIR, name)
+        os.makedirs(bdir, exist_ok=True)
+        load(name=name, sources=[src], build_directory=bdir, verbose=verbose,
+             extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"],
+             extra_cflags=["-O3"])
+        built[name] = os.path.join(bdir, name + ".so")
+    return built
+
+
+def load_ref(name):
+    """Import a reference engine built by build_ref() (no rebuild, no sources
+    needed).  Returns None when it was not built."""
+    path = os.path.join(REF_DIR, name, name + ".so")
+    if not os.path.exists(path):
+        return None
+    import torch  # noqa: F401  (the extension links against libtorch)
+
+    loader = importlib.machinery.ExtensionFileLoader(name, path)
+    spec = importlib.util.spec_from_file_location(name, path, loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    a = ap.parse_args()
+    print(build_ref(a.reference, verbose=True))
+    sys.exit(0)

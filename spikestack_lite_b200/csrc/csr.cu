@@ -1,0 +1,304 @@
+// Spike -> CSR compaction for T planes in one launch (single pass over S).
+//
+// Replaces the reference engine's csr_build_kernel + scan_blocks_kernel +
+// offscan_add_kernel + csr_compact_kernel (sparse_linear.cu:251-369).  Same
+// predicate (S > 0, so negatives and NaN are dropped), same ascending column
+// order, same int32 row_offsets per plane; unlike the reference it is correct
+// for any number of rows (its block-offset scan stops at 65536 rows) and it
+// reads S exactly once:
+//
+//   phase A  each warp ballots its rows 32 columns at a time into a bitmap
+//            held in shared memory and counts the nonzeros per row;
+//   phase B  the tile total is published and the tile's exclusive prefix is
+//            found by a decoupled look-back over earlier tiles (tile ids are
+//            handed out in launch order by an atomic counter, so every tile a
+//            CTA waits on is already resident; every wait is bounded);
+//   phase C  row_ptr / nnz_row are written and the bitmap is expanded into
+//            column indices with coalesced stores (one 32-column word per
+//            warp step), values gathered from S.
+//
+// Tiles never straddle planes; the first tile of plane t publishes the plane
+// base so that row_ptr is relative to the plane (as in the reference) while
+// col_idx holds the planes back to back.
+#include "spk_common.cuh"
+
+namespace spk {
+
+struct ScanState {
+  unsigned int tile_counter;
+  unsigned int pad[63];
+  // followed by: uint64_t tile_desc[num_tiles]; uint64_t plane_desc[T]; uint8_t tile_flags[num_tiles]
+};
+
+constexpr uint64_t kDescAgg = 1ull << 62;
+constexpr uint64_t kDescIncl = 2ull << 62;
+constexpr uint64_t kDescValueMask = (1ull << 62) - 1;
+
+struct CsrLayout {
+  int T;
+  int64_t M;
+  int K, KW;
+  int rows_per_tile;
+  int64_t tiles_per_plane, num_tiles;
+  size_t desc_off, plane_desc_off, flags_off, total;
+};
+
+inline CsrLayout csr_layout(int T, int64_t M, int K) {
+  CsrLayout L{};
+  L.T = T;
+  L.M = M;
+  L.K = K;
+  L.KW = (K + 31) / 32;
+  int rt = 16384 / (L.KW > 0 ? L.KW : 1);
+  rt = rt > 128 ? 128 : rt;
+  rt = rt < 8 ? 8 : rt;
+  L.rows_per_tile = rt & ~7;
+  L.tiles_per_plane = ceil_div(M, L.rows_per_tile);
+  L.num_tiles = L.tiles_per_plane * T;
+  L.desc_off = sizeof(ScanState);
+  L.plane_desc_off = L.desc_off + sizeof(uint64_t) * L.num_tiles;
+  L.flags_off = L.plane_desc_off + sizeof(uint64_t) * T;
+  L.total = align_up(L.flags_off + L.num_tiles, 256);
+  return L;
+}
+
+struct CsrArgs {
+  const float* S;          // [T*M, K]
+  int T;
+  int64_t M;
+  int K, KW, rows_per_tile;
+  int64_t tiles_per_plane, num_tiles;
+  int32_t* nnz_row;        // [T*M] or null
+  int32_t* row_ptr;        // [T*(M+1)]
+  int32_t* col_idx;        // capacity col_capacity
+  float* values;           // capacity col_capacity or null
+  int64_t* plane_ptr;      // [T+1]
+  int64_t col_capacity;
+  ScanState* state;
+  uint64_t* tile_desc;
+  uint64_t* plane_desc;
+  uint8_t* tile_flags;     // [num_tiles]: 1 if the tile holds a positive value != 1
+};
+
+__device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
+  uint64_t d = ld_relaxed_u64(p);
+  if ((d >> 62) != 0) return d;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    d = ld_relaxed_u64(p);
+    if ((d >> 62) != 0) return d;
+    if ((it & 31u) == 0 && global_ns() - t0 > kSpinLimitNs) {
+      report_device_error(SPK_DEV_SCAN_TIMEOUT);
+      ok = false;
+      return kDescIncl;  // value 0
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
+  extern __shared__ __align__(16) uint32_t smem_u32buf[];
+  const int RT = a.rows_per_tile;
+  uint32_t* bm = smem_u32buf;                    // [RT][KW]
+  int32_t* cnt = reinterpret_cast<int32_t*>(bm + (size_t)RT * a.KW);  // [RT]
+  int32_t* pre = cnt + RT;                       // [RT] exclusive prefix inside the tile
+  __shared__ int64_t s_excl, s_base;
+  __shared__ unsigned int s_tile;
+  __shared__ int s_nonunit;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    s_tile = atomicAdd(&a.state->tile_counter, 1u);
+    s_nonunit = 0;
+  }
+  __syncthreads();
+  const int64_t tile = s_tile;
+  const bool valid_tile = tile < a.num_tiles;
+  const int plane = valid_tile ? (int)(tile / a.tiles_per_plane) : 0;
+  const int64_t tip = valid_tile ? tile % a.tiles_per_plane : 0;
+  const int64_t row0 = tip * RT;  // row within plane
+  const int rows = valid_tile ? (int)min64(RT, a.M - row0) : 0;
+  const float* Sp = a.S + ((int64_t)plane * a.M + row0) * a.K;
+
+  // ---- phase A: ballot rows into the shared bitmap
+  bool nonunit = false;
+  for (int r = warp; r < RT; r += 8) {
+    int c = 0;
+    if (r < rows) {
+      const float* row = Sp + (int64_t)r * a.K;
+      for (int w0 = 0; w0 < a.KW; w0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = (w0 + j) * 32 + lane;
+          v[j] = (w0 + j < a.KW && col < a.K) ? __ldg(row + col) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool nz = v[j] > 0.0f;
+          nonunit |= nz && (v[j] != 1.0f);
+          const uint32_t bits = __ballot_sync(0xffffffffu, nz);
+          if (w0 + j < a.KW) {
+            if (lane == 0) bm[r * a.KW + w0 + j] = bits;
+            c += __popc(bits);
+          }
+        }
+      }
+    }
+    if (lane == 0) cnt[r] = c;
+  }
+  if (__any_sync(0xffffffffu, nonunit) && lane == 0) s_nonunit = 1;
+  __syncthreads();
+
+  // ---- phase B: in-tile exclusive prefix (warp 0), then the look-back (thread 0)
+  if (warp == 0) {
+    int64_t running = 0;
+    for (int base = 0; base < RT; base += 32) {
+      const int r = base + lane;
+      const int v = (r < RT) ? cnt[r] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (r < RT) pre[r] = (int)running + incl - v;
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0 && valid_tile) {
+      const int64_t agg = running;
+      bool ok = true;
+      int64_t excl = 0;
+      if (tile == 0) {
+        st_relaxed_u64(&a.tile_desc[0], kDescIncl | (uint64_t)agg);
+      } else {
+        st_relaxed_u64(&a.tile_desc[tile], kDescAgg | (uint64_t)agg);
+        for (int64_t j = tile - 1; j >= 0 && ok; --j) {
+          const uint64_t d = spin_desc(&a.tile_desc[j], ok);
+          excl += (int64_t)(d & kDescValueMask);
+          if ((d >> 62) == 2) break;
+        }
+        st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
+      }
+      int64_t base;
+      if (tip == 0) {
+        base = excl;
+        st_relaxed_u64(&a.plane_desc[plane], kDescIncl | (uint64_t)base);
+        a.plane_ptr[plane] = base;
+        a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
+      } else {
+        const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
+        base = (int64_t)(d & kDescValueMask);
+      }
+      if (plane == a.T - 1 && tip == a.tiles_per_plane - 1) a.plane_ptr[a.T] = excl + agg;
+      a.tile_flags[tile] = s_nonunit ? 1 : 0;
+      s_excl = excl;
+      s_base = base;
+    }
+  }
+  __syncthreads();
+
+  // ---- phase C: row pointers and column indices
+  if (valid_tile) {
+    const int64_t excl = s_excl, rel = s_excl - s_base;
+    int32_t* rp = a.row_ptr + (int64_t)plane * (a.M + 1) + row0 + 1;
+    int32_t* nr = a.nnz_row ? a.nnz_row + (int64_t)plane * a.M + row0 : nullptr;
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+      rp[r] = (int32_t)(rel + pre[r] + cnt[r]);
+      if (nr) nr[r] = cnt[r];
+    }
+    const uint32_t lt = (1u << lane) - 1u;
+    bool overflow = false;
+    for (int r = warp; r < rows; r += 8) {
+      int64_t pos = excl + pre[r];
+      const uint32_t* bw = bm + r * a.KW;
+      const float* row = Sp + (int64_t)r * a.K;
+      for (int w = 0; w < a.KW; ++w) {
+        const uint32_t bits = bw[w];
+        if (bits == 0u) continue;
+        if ((bits >> lane) & 1u) {
+          const int64_t p = pos + __popc(bits & lt);
+          if (p < a.col_capacity) {
+            a.col_idx[p] = w * 32 + lane;
+            if (a.values) a.values[p] = row[w * 32 + lane];
+          } else {
+            overflow = true;
+          }
+        }
+        pos += __popc(bits);
+      }
+    }
+    if (__any_sync(0xffffffffu, overflow) && lane == 0) report_device_error(SPK_DEV_CSR_OVERFLOW);
+  }
+
+}
+
+// Launch helper shared by every entry point that emits CSR.
+int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
+                    int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
+                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out) {
+  const CsrLayout L = csr_layout(T, M, K);
+  CsrArgs a{};
+  a.S = S;
+  a.T = T;
+  a.M = M;
+  a.K = K;
+  a.KW = L.KW;
+  a.rows_per_tile = L.rows_per_tile;
+  a.tiles_per_plane = L.tiles_per_plane;
+  a.num_tiles = L.num_tiles;
+  a.nnz_row = nnz_row;
+  a.row_ptr = row_ptr;
+  a.col_idx = col_idx;
+  a.values = values;
+  a.plane_ptr = plane_ptr;
+  a.col_capacity = col_capacity;
+  char* base = static_cast<char*>(ws);
+  a.state = reinterpret_cast<ScanState*>(base);
+  a.tile_desc = reinterpret_cast<uint64_t*>(base + L.desc_off);
+  a.plane_desc = reinterpret_cast<uint64_t*>(base + L.plane_desc_off);
+  a.tile_flags = reinterpret_cast<uint8_t*>(base + L.flags_off);
+  const size_t smem = (size_t)L.rows_per_tile * L.KW * 4 + (size_t)L.rows_per_tile * 8;
+  if (smem > 48 * 1024) {
+    SPK_CUDA_TRY(cudaFuncSetAttribute(csr_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  // The tile counter and the look-back descriptors start from zero on every
+  // launch (stream-ordered), so the workspace needs no persistent state and
+  // can be shared with any other use between calls.
+  SPK_CUDA_TRY(cudaMemsetAsync(base, 0, L.flags_off, stream));
+  prof_before(SPK_KERNEL_CSR_SCAN, stream);
+  csr_scan_kernel<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
+  prof_after(SPK_KERNEL_CSR_SCAN, stream);
+  SPK_LAUNCH_CHECK();
+  count_launch(1);
+  if (tile_flags_out) *tile_flags_out = a.tile_flags;
+  if (layout_out) *layout_out = L;
+  return SPK_OK;
+}
+
+int check_csr_shape(int T, int64_t M, int K) {
+  SPK_REQUIRE(T >= 1 && M >= 1 && K >= 1, "invalid shape T=%d M=%lld K=%d", T, (long long)M, K);
+  SPK_REQUIRE(K <= 131072, "K=%d exceeds the supported maximum of 131072 columns", K);
+  SPK_REQUIRE((int64_t)M * K < (int64_t)INT32_MAX, "a plane of M*K=%lld entries overflows int32 row offsets",
+              (long long)M * K);
+  SPK_REQUIRE(csr_layout(T, M, K).num_tiles < (int64_t)INT32_MAX, "too many row tiles");
+  return SPK_OK;
+}
+
+}  // namespace spk
+
+extern "C" size_t spk_csr_workspace_bytes(int T, int64_t M, int K) {
+  if (T < 1 || M < 1 || K < 1) return 0;
+  return spk::csr_layout(T, M, K).total;
+}
+
+extern "C" int spk_csr_compact(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
+                               int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity,
+                               void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  int rc = spk::check_csr_shape(T, M, K);
+  if (rc) return rc;
+  SPK_REQUIRE(S && row_ptr && col_idx && plane_ptr, "S, row_ptr, col_idx and plane_ptr must be non-null");
+  if (workspace == nullptr || workspace_bytes < spk::csr_layout(T, M, K).total)
+    return spk::fail(SPK_EWORKSPACE, "workspace of %zu bytes required", spk::csr_layout(T, M, K).total);
+  return spk::launch_csr_scan(S, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr, col_capacity, workspace,
+                              (cudaStream_t)stream, nullptr, nullptr);
+}

@@ -1,0 +1,9 @@
+// Single translation unit of libspk_b200.so: the kernels share device state
+// (the device error word) and inline helpers without relocatable device code.
+#include "runtime.cu"
+#include "csr.cu"
+#include "spmm_csr.cu"
+#include "spike_linear_tc.cu"
+#include "spike_linear.cu"
+#include "attention.cu"
+#include "gsmc.cu"

@@ -1,0 +1,172 @@
+// Entry points of the spike-linear path: the new multi-plane C ABI and the
+// two reference-compatible ops (sparse_forward / sparse_multistep_forward).
+//
+// Orchestration per call (one stream, no host synchronisation):
+//   dense branch:  W image (bf16 hi/lo, pre-swizzled)  ->  tcgen05 kernel
+//                  [-> CSR scan when CSR outputs are requested]
+//   CSR branch:    CSR scan of all planes  ->  CSR SpMM with the weight tile
+//                  held in shared memory across all planes
+#include "spk_common.cuh"
+
+namespace spk {
+
+// from csr.cu / spmm_csr.cu / spike_linear_tc.cu (single translation unit)
+struct CsrLayout;
+int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
+                    int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
+                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out);
+
+struct SlLayout {
+  size_t csr_state;     // look-back state for the scan (zero-initialised once)
+  size_t img;           // W image (dense branch)
+  size_t csr_rowptr;    // internal CSR when the caller did not ask for it (CSR branch)
+  size_t csr_planeptr;
+  size_t csr_cols;
+  int64_t csr_capacity;
+  size_t total;
+};
+
+inline int resolve_branch(int branch, int K, int N, const void* S) {
+  if (branch == SPK_BRANCH_DENSE || branch == SPK_BRANCH_CSR) return branch;
+  // Dense unless the tcgen05 path cannot take the shape.  The dense branch is
+  // HBM-bound for the narrow layers of the model (N <= 512) at any density,
+  // so it never loses there; the CSR branch only wins on wide layers at very
+  // low density, which a caller selects explicitly.
+  return tc_supported(K, N, S) ? SPK_BRANCH_DENSE : SPK_BRANCH_CSR;
+}
+
+inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool internal_csr) {
+  SlLayout L{};
+  size_t off = 0;
+  L.csr_state = off;
+  off += align_up(csr_layout(T, M, K).total, 256);
+  L.img = off;
+  off += align_up(tc_plan(K, N, w_dtype).img_bytes, 1024);
+  if (internal_csr) {
+    L.csr_rowptr = off;
+    off += align_up(sizeof(int32_t) * (size_t)T * (M + 1), 256);
+    L.csr_planeptr = off;
+    off += align_up(sizeof(int64_t) * (size_t)(T + 1), 256);
+    L.csr_cols = off;
+    L.csr_capacity = (int64_t)T * M * K;
+    off += align_up(sizeof(int32_t) * (size_t)L.csr_capacity, 256);
+  }
+  L.total = off;
+  return L;
+}
+
+int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t sk, int64_t sn,
+                      int N, const float* bias, float* Y, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx,
+                      float* values, int64_t* plane_ptr, int64_t col_capacity, int branch, void* ws,
+                      size_t ws_bytes, cudaStream_t stream) {
+  int rc = check_csr_shape(T, M, K);
+  if (rc) return rc;
+  SPK_REQUIRE(N >= 1, "N must be positive");
+  SPK_REQUIRE(S && W && Y, "S, W and Y must be non-null");
+  SPK_REQUIRE(w_dtype == SPK_F32 || w_dtype == SPK_BF16, "w_dtype must be SPK_F32 or SPK_BF16");
+  const bool want_csr = row_ptr != nullptr || col_idx != nullptr || plane_ptr != nullptr;
+  SPK_REQUIRE(!want_csr || (row_ptr && col_idx && plane_ptr), "CSR outputs need row_ptr, col_idx and plane_ptr");
+  branch = resolve_branch(branch, K, N, S);
+  if (branch == SPK_BRANCH_DENSE)
+    SPK_REQUIRE(tc_supported(K, N, S), "dense branch needs K %% 4 == 0 and a 16-byte aligned S");
+  const bool internal_csr = (branch == SPK_BRANCH_CSR) && !want_csr;
+  const SlLayout L = sl_layout(T, M, K, N, w_dtype, internal_csr);
+  if (ws == nullptr || ws_bytes < L.total)
+    return fail(SPK_EWORKSPACE, "workspace of %zu bytes required (got %zu)", L.total, ws_bytes);
+  char* wsb = static_cast<char*>(ws);
+
+  if (branch == SPK_BRANCH_DENSE) {
+    const TcPlan p = tc_plan(K, N, w_dtype);
+    unsigned char* img = reinterpret_cast<unsigned char*>(wsb + L.img);
+    rc = launch_w_image(W, w_dtype, sk, sn, K, N, p, img, stream);
+    if (rc) return rc;
+    rc = launch_tc(S, (int64_t)T * M, K, N, p, img, bias, Y, stream);
+    if (rc) return rc;
+    if (want_csr) {
+      rc = launch_csr_scan(S, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr, col_capacity,
+                           wsb + L.csr_state, stream, nullptr, nullptr);
+    }
+    return rc;
+  }
+  // CSR branch
+  int32_t* rp = row_ptr;
+  int32_t* ci = col_idx;
+  int64_t* pp = plane_ptr;
+  int64_t cap = col_capacity;
+  if (internal_csr) {
+    rp = reinterpret_cast<int32_t*>(wsb + L.csr_rowptr);
+    pp = reinterpret_cast<int64_t*>(wsb + L.csr_planeptr);
+    ci = reinterpret_cast<int32_t*>(wsb + L.csr_cols);
+    cap = L.csr_capacity;
+  }
+  const uint8_t* flags = nullptr;
+  CsrLayout cl{};
+  rc = launch_csr_scan(S, T, M, K, nnz_row, rp, ci, values, pp, cap, wsb + L.csr_state, stream, &flags, &cl);
+  if (rc) return rc;
+  return launch_spmm_csr(rp, pp, ci, values, S, flags, cl.rows_per_tile, cl.tiles_per_plane, W, w_dtype, sk, sn,
+                         bias, Y, T, M, K, N, cap, stream);
+}
+
+}  // namespace spk
+
+extern "C" size_t spk_spike_linear_workspace_bytes(int T, int64_t M, int K, int N, int w_dtype) {
+  if (T < 1 || M < 1 || K < 1 || N < 1) return 0;
+  // enough for either branch, including the CSR branch's internal CSR
+  return spk::sl_layout(T, M, K, N, w_dtype, true).total;
+}
+
+extern "C" int spk_spike_linear(const float* S, int T, int64_t M, int K, const void* W, int w_dtype,
+                                int64_t w_stride_k, int64_t w_stride_n, int N, const float* bias, float* Y,
+                                int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
+                                int64_t* plane_ptr, int64_t col_capacity, int branch, void* workspace,
+                                size_t workspace_bytes, spk_stream_t stream) {
+  return spk::spike_linear_impl(S, T, M, K, W, w_dtype, w_stride_k, w_stride_n, N, bias, Y, nnz_row, row_ptr,
+                                col_idx, values, plane_ptr, col_capacity, branch, workspace, workspace_bytes,
+                                (cudaStream_t)stream);
+}
+
+extern "C" size_t spk_sparse_forward_workspace_bytes(int T, int64_t B, int I, int O) {
+  if (T < 1 || B < 1 || I < 1 || O < 1) return 0;
+  return spk_spike_linear_workspace_bytes(T, B, I, O, SPK_F32) + 1024;
+}
+
+// The reference ops leave the CSR of plane T-1 in the caller's buffers: the
+// product runs over all planes, then the last plane's CSR is written into
+// nnz_per_row / row_offsets / col_indices / values.
+static int reference_multistep(const float* x, int T, int64_t B, int I, const float* weightT, int O,
+                               int32_t* nnz_per_row, int32_t* row_offsets, int32_t* col_indices, float* values,
+                               int64_t col_capacity, float* out, int branch, void* ws, size_t ws_bytes,
+                               cudaStream_t stream) {
+  int rc = spk::check_csr_shape(T, B, I);
+  if (rc) return rc;
+  SPK_REQUIRE(x && weightT && out, "input, weightT and output must be non-null");
+  SPK_REQUIRE(nnz_per_row && row_offsets && col_indices && values, "CSR buffers must be non-null");
+  SPK_REQUIRE(O >= 1, "O must be positive");
+  const size_t need = spk_sparse_forward_workspace_bytes(T, B, I, O);
+  if (ws == nullptr || ws_bytes < need) return spk::fail(SPK_EWORKSPACE, "workspace of %zu bytes required", need);
+  // plane pointer pair of the last plane lives at the end of the workspace
+  int64_t* pp = reinterpret_cast<int64_t*>(static_cast<char*>(ws) + need - 1024);
+  rc = spk::spike_linear_impl(x, T, B, I, weightT, SPK_F32, O, 1, O, nullptr, out, nullptr, nullptr, nullptr,
+                              nullptr, nullptr, 0, branch, ws, need - 1024, stream);
+  if (rc) return rc;
+  const float* last = x + (int64_t)(T - 1) * B * I;
+  return spk::launch_csr_scan(last, 1, B, I, nnz_per_row, row_offsets, col_indices, values, pp, col_capacity, ws,
+                              stream, nullptr, nullptr);
+}
+
+extern "C" int spk_sparse_forward(const float* input, int64_t B, int I, const float* weightT, int O,
+                                  int32_t* nnz_per_row, int32_t* row_offsets, int32_t* col_indices, float* values,
+                                  int64_t col_capacity, float* output, int branch, void* workspace,
+                                  size_t workspace_bytes, spk_stream_t stream) {
+  return reference_multistep(input, 1, B, I, weightT, O, nnz_per_row, row_offsets, col_indices, values,
+                             col_capacity, output, branch, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int spk_sparse_multistep_forward(const float* dense_input, int T, int64_t B, int I,
+                                            const float* weightT, int O, int32_t* nnz_per_row,
+                                            int32_t* row_offsets, int32_t* col_indices, float* values,
+                                            int64_t col_capacity, float* output, int branch, void* workspace,
+                                            size_t workspace_bytes, spk_stream_t stream) {
+  return reference_multistep(dense_input, T, B, I, weightT, O, nnz_per_row, row_offsets, col_indices, values,
+                             col_capacity, output, branch, workspace, workspace_bytes, (cudaStream_t)stream);
+}

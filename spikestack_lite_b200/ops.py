@@ -1,0 +1,278 @@
+"""Tensor-level ops over the C ABI (torch tensors in, torch tensors out).
+
+Every op validates its tensors (CUDA, float32, contiguous where the kernel
+needs it), passes raw pointers and the current stream of the tensors' device
+to libspk_b200.so and raises ``EngineError`` (a RuntimeError) on any failure.
+"""
+import torch
+
+from . import _lib
+from ._lib import EngineError, check, ptr, require_cuda, require_f32, stream_of
+
+
+def _branch(b):
+    if isinstance(b, int):
+        return b
+    try:
+        return _lib.BRANCHES[b]
+    except KeyError:
+        raise EngineError(f"unknown branch {b!r} (auto, dense or csr)") from None
+
+
+def _contig(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ----------------------------------------------------------------- spike -> CSR
+def csr_compact(S, values=True):
+    """Per-plane CSR of S [T, M, K] (or [M, K] as one plane).
+
+    Returns a dict with nnz_row [T, M], row_ptr [T, M+1] (int32, relative to
+    each plane), col_idx (int32, planes back to back), values (float32 or
+    None) and plane_ptr [T+1] (int64).  One launch for all planes (plus a
+    small device->host read of the total to size the outputs)."""
+    require_cuda(S, what="csr_compact")
+    require_f32(S, what="csr_compact")
+    S = _contig(S)
+    if S.dim() == 2:
+        S = S.unsqueeze(0)
+    T, M, K = S.shape
+    lib = _lib.load()
+    dev = S.device
+    nnz_row = torch.empty(T, M, dtype=torch.int32, device=dev)
+    row_ptr = torch.empty(T, M + 1, dtype=torch.int32, device=dev)
+    plane_ptr = torch.empty(T + 1, dtype=torch.int64, device=dev)
+    cap = int((S > 0).sum().item())
+    col_idx = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    vals = torch.empty(max(cap, 1), dtype=torch.float32, device=dev) if values else None
+    ws, wsn = _lib.workspace(dev, lib.spk_csr_workspace_bytes(T, M, K))
+    check(lib.spk_csr_compact(ptr(S), T, M, K, ptr(nnz_row), ptr(row_ptr), ptr(col_idx), ptr(vals),
+                              ptr(plane_ptr), cap, ws, wsn, stream_of(S)), "spk_csr_compact")
+    return {"nnz_row": nnz_row, "row_ptr": row_ptr, "col_idx": col_idx[:cap],
+            "values": None if vals is None else vals[:cap], "plane_ptr": plane_ptr}
+
+
+# ------------------------------------------------------------------ spike-linear
+def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=None):
+    """Y[..., n] = sum_{k: S[..., k] > 0} S[..., k] W[k, n] (+ bias) for S [T, M, K]
+    (or [M, K]).  W is given either as an nn.Linear ``weight`` [N, K] or as
+    ``weightT`` [K, N] (the reference op layout), float32 or bfloat16.
+
+    ``csr``: None, or a dict with preallocated int32/int64 buffers
+    {nnz_row [T*M], row_ptr [T*(M+1)], col_idx [cap], plane_ptr [T+1],
+    values [cap] (optional)} that receive the per-plane CSR."""
+    require_cuda(S, weight, weightT, bias, what="spike_linear")
+    require_f32(S, bias, what="spike_linear")
+    if (weight is None) == (weightT is None):
+        raise EngineError("spike_linear: pass exactly one of weight [N, K] or weightT [K, N]")
+    squeeze = S.dim() == 2
+    S = _contig(S)
+    if squeeze:
+        S = S.unsqueeze(0)
+    if S.dim() != 3:
+        raise EngineError(f"spike_linear: S must be [T, M, K] or [M, K], got {tuple(S.shape)}")
+    T, M, K = S.shape
+    W = weight if weight is not None else weightT
+    if W.dtype not in (torch.float32, torch.bfloat16):
+        raise EngineError(f"spike_linear: weight dtype {W.dtype} not supported (float32 or bfloat16)")
+    if weight is not None:
+        N, Kw = weight.shape
+        sk, sn = weight.stride(1), weight.stride(0)
+    else:
+        Kw, N = weightT.shape
+        sk, sn = weightT.stride(0), weightT.stride(1)
+    if Kw != K:
+        raise EngineError(f"spike_linear: weight K={Kw} does not match input K={K}")
+    if bias is not None:
+        bias = _contig(bias)
+        if bias.numel() != N:
+            raise EngineError("spike_linear: bias must have N elements")
+    wdt = _lib.SPK_BF16 if W.dtype == torch.bfloat16 else _lib.SPK_F32
+    lib = _lib.load()
+    Y = torch.empty(T, M, N, dtype=torch.float32, device=S.device)
+    c = csr or {}
+    cap = c["col_idx"].numel() if c else 0
+    ws, wsn = _lib.workspace(S.device, lib.spk_spike_linear_workspace_bytes(T, M, K, N, wdt))
+    check(lib.spk_spike_linear(ptr(S), T, M, K, ptr(W), wdt, sk, sn, N, ptr(bias), ptr(Y),
+                               ptr(c.get("nnz_row")), ptr(c.get("row_ptr")), ptr(c.get("col_idx")),
+                               ptr(c.get("values")), ptr(c.get("plane_ptr")), cap, _branch(branch), ws, wsn,
+                               stream_of(S)), "spk_spike_linear")
+    return Y[0] if squeeze else Y
+
+
+def alloc_csr(T, M, K, device, capacity=None, values=False):
+    """Preallocated per-plane CSR buffers for spike_linear(csr=...)."""
+    cap = int(capacity if capacity is not None else T * M * K)
+    d = {
+        "nnz_row": torch.empty(T * M, dtype=torch.int32, device=device),
+        "row_ptr": torch.empty(T * (M + 1), dtype=torch.int32, device=device),
+        "col_idx": torch.empty(max(cap, 1), dtype=torch.int32, device=device),
+        "plane_ptr": torch.empty(T + 1, dtype=torch.int64, device=device),
+    }
+    if values:
+        d["values"] = torch.empty(max(cap, 1), dtype=torch.float32, device=device)
+    return d
+
+
+def sparse_multistep_forward(dense_input, weightT, nnz_per_row, row_offsets, col_indices, values, T,
+                             branch="auto"):
+    """The reference op (sparse_linear.cu:645-691): dense_input [T, B, I],
+    weightT [I, O] -> [T, B, O]; the CSR buffers receive plane T-1's CSR."""
+    require_cuda(dense_input, weightT, nnz_per_row, row_offsets, col_indices, values,
+                 what="sparse_multistep_forward")
+    require_f32(dense_input, weightT, values, what="sparse_multistep_forward")
+    x = _contig(dense_input)
+    T = int(T)
+    if x.dim() != 3 or x.shape[0] != T:
+        x = x.reshape(T, -1, x.shape[-1])
+    _, B, I = x.shape
+    wT = _contig(weightT)
+    O = wT.shape[1]
+    if wT.shape[0] != I:
+        raise EngineError(f"sparse_multistep_forward: weightT has {wT.shape[0]} rows, input has {I} features")
+    cap = min(col_indices.numel(), values.numel())
+    out = torch.empty(T, B, O, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(x.device, lib.spk_sparse_forward_workspace_bytes(T, B, I, O))
+    check(lib.spk_sparse_multistep_forward(ptr(x), T, B, I, ptr(wT), O, ptr(nnz_per_row), ptr(row_offsets),
+                                           ptr(col_indices), ptr(values), cap, ptr(out), _branch(branch), ws, wsn,
+                                           stream_of(x)), "spk_sparse_multistep_forward")
+    return out
+
+
+def sparse_forward(input, weightT, nnz_per_row, row_offsets, col_indices, values, branch="auto"):
+    """The reference op (sparse_linear.cu:594-631): input [B, I] -> [B, O]."""
+    require_cuda(input, weightT, nnz_per_row, row_offsets, col_indices, values, what="sparse_forward")
+    require_f32(input, weightT, values, what="sparse_forward")
+    x = _contig(input)
+    B, I = x.shape
+    wT = _contig(weightT)
+    O = wT.shape[1]
+    if wT.shape[0] != I:
+        raise EngineError(f"sparse_forward: weightT has {wT.shape[0]} rows, input has {I} features")
+    cap = min(col_indices.numel(), values.numel())
+    out = torch.empty(B, O, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(x.device, lib.spk_sparse_forward_workspace_bytes(1, B, I, O))
+    check(lib.spk_sparse_forward(ptr(x), B, I, ptr(wT), O, ptr(nnz_per_row), ptr(row_offsets), ptr(col_indices),
+                                 ptr(values), cap, ptr(out), _branch(branch), ws, wsn, stream_of(x)),
+          "spk_sparse_forward")
+    return out
+
+
+def dense_to_csr_gpu(dense_input):
+    """The reference op dense_to_csr_gpu (sparse_linear.cu:563-588):
+    [B, I] -> [row_offsets [B+1], col_indices [B*I], values [B*I]]."""
+    require_cuda(dense_input, what="dense_to_csr_gpu")
+    require_f32(dense_input, what="dense_to_csr_gpu")
+    x = _contig(dense_input)
+    B, I = x.shape
+    dev = x.device
+    row_ptr = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    col_idx = torch.empty(B * I, dtype=torch.int32, device=dev)
+    vals = torch.empty(B * I, dtype=torch.float32, device=dev)
+    plane_ptr = torch.empty(2, dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(dev, lib.spk_csr_workspace_bytes(1, B, I))
+    check(lib.spk_csr_compact(ptr(x), 1, B, I, None, ptr(row_ptr), ptr(col_idx), ptr(vals), ptr(plane_ptr), B * I,
+                              ws, wsn, stream_of(x)), "spk_csr_compact")
+    return [row_ptr, col_idx, vals]
+
+
+# ---------------------------------------------------------------------- attention
+def apply_channel_decay(k, lam):
+    """k_w = k * lam ** (N-1-n) (attention_cuda.cu:42-77)."""
+    require_cuda(k, lam, what="apply_channel_decay")
+    require_f32(k, lam, what="apply_channel_decay")
+    if k.dim() < 2:
+        raise EngineError("apply_channel_decay: k must have at least 2 dimensions")
+    k = _contig(k)
+    lam = _contig(lam)
+    d, N = k.shape[-1], k.shape[-2]
+    if lam.dim() != 1 or lam.numel() != d:
+        raise EngineError("apply_channel_decay: lam must be 1D tensor of size d matching k.size(-1)")
+    out = torch.empty_like(k)
+    if k.numel() == 0:
+        return out
+    check(_lib.load().spk_apply_channel_decay(ptr(k), ptr(lam), k.numel() // (N * d), N, d, ptr(out), stream_of(k)),
+          "spk_apply_channel_decay")
+    return out
+
+
+def fused_normalize_attention(numer, denom, eps):
+    """numer / (denom + eps) elementwise (attention_cuda.cu:79-107)."""
+    require_cuda(numer, denom, what="fused_normalize_attention")
+    require_f32(numer, denom, what="fused_normalize_attention")
+    if denom.numel() < numer.numel():
+        raise EngineError("fused_normalize_attention: denom must have at least as many elements as numer")
+    numer = _contig(numer)
+    denom = _contig(denom)
+    out = torch.empty_like(numer)
+    check(_lib.load().spk_normalize_attention(ptr(numer), ptr(denom), numer.numel(), float(eps), ptr(out),
+                                              stream_of(numer)), "spk_normalize_attention")
+    return out
+
+
+def spiking_attention(q, k, v, lam, heads, eps=1e-6):
+    """Fused spiking linear attention: q, k, v spikes [..., L, d] (d = heads*dh)
+    -> normalised attention [..., L, d] (the o_proj input of
+    AstrocyteHebbianAttention, attention.py:120-135)."""
+    require_cuda(q, k, v, lam, what="spiking_attention")
+    require_f32(q, k, v, lam, what="spiking_attention")
+    shape = q.shape
+    L, d = shape[-2], shape[-1]
+    if k.shape != shape or v.shape != shape:
+        raise EngineError("spiking_attention: q, k and v must have the same shape")
+    if d % heads:
+        raise EngineError("spiking_attention: d_model must be divisible by heads")
+    dh = d // heads
+    q, k, v, lam = (_contig(t) for t in (q, k, v, lam))
+    BT = q.numel() // (L * d)
+    out = torch.empty(shape, dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(q.device, lib.spk_attention_workspace_bytes(BT, L, heads, dh))
+    check(lib.spk_spiking_attention(ptr(q), ptr(k), ptr(v), ptr(lam), BT, L, heads, dh, float(eps), ptr(out), ws,
+                                    wsn, stream_of(q)), "spk_spiking_attention")
+    return out
+
+
+# --------------------------------------------------------------------------- GSMC
+def fused_gsmc_step(gi, gr, wd, bias, m, s, heat, v_th, gate_scale, adaptive_threshold, beta_adapt):
+    """One GSMC step (gsmc_cuda.cu:79-127); updates m, s, heat in place and
+    returns the new spikes [M, d]."""
+    require_cuda(gi, gr, wd, bias, m, s, heat, what="fused_gsmc_step")
+    require_f32(gi, gr, wd, bias, m, s, heat, what="fused_gsmc_step")
+    for t in (gi, gr, wd, bias, m, s, heat):
+        if not t.is_contiguous():
+            raise EngineError("fused_gsmc_step: inputs and state tensors must be contiguous")
+    M, d = gi.shape[0], wd.shape[-1]
+    if gi.shape[-1] != 4 * d or gr.shape[-1] != 4 * d:
+        raise EngineError("fused_gsmc_step: gi and gr must be of shape (M, 4*d)")
+    if bias.numel() != 4 * d:
+        raise EngineError("fused_gsmc_step: bias must have 4*d elements")
+    if m.numel() != M * d or s.numel() != M * d or heat.numel() != M * d:
+        raise EngineError("fused_gsmc_step: m, s and heat must be of size (M, d)")
+    out = torch.empty(M, d, dtype=torch.float32, device=gi.device)
+    check(_lib.load().spk_gsmc_step(ptr(gi), ptr(gr), ptr(wd), ptr(bias), ptr(m), ptr(s), ptr(heat), ptr(out), M, d,
+                                    float(v_th), float(gate_scale), int(bool(adaptive_threshold)),
+                                    float(beta_adapt), stream_of(gi)), "spk_gsmc_step")
+    return out
+
+
+def gsmc_forward(gi_all, wd_all, w_rec, bias, v_th=1.0, gate_scale=4.0, adaptive=True, beta=0.8, pool="mean",
+                 return_planes=False):
+    """The eval-mode GSMC recurrence (gsmc.py:96-148) over precomputed input
+    projections gi_all [T, M, 4d] and wd_all [T, M, d]; w_rec is the W_rec
+    nn.Linear weight [4d, d].  Returns pooled [M, d] (and the planes [T, M, d])."""
+    require_cuda(gi_all, wd_all, w_rec, bias, what="gsmc_forward")
+    require_f32(gi_all, wd_all, w_rec, bias, what="gsmc_forward")
+    gi_all, wd_all, w_rec, bias = (_contig(t) for t in (gi_all, wd_all, w_rec, bias))
+    T, M, d = wd_all.shape
+    pooled = torch.empty(M, d, dtype=torch.float32, device=gi_all.device)
+    planes = torch.empty(T, M, d, dtype=torch.float32, device=gi_all.device) if return_planes else None
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(gi_all.device, lib.spk_gsmc_workspace_bytes(M, d))
+    check(lib.spk_gsmc_forward(ptr(gi_all), ptr(wd_all), ptr(w_rec), ptr(bias), T, M, d, float(v_th),
+                               float(gate_scale), int(bool(adaptive)), float(beta), 1 if pool == "mean" else 0,
+                               ptr(planes), ptr(pooled), ws, wsn, stream_of(gi_all)), "spk_gsmc_forward")
+    return (pooled, planes) if return_planes else pooled

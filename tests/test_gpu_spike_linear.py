@@ -1,0 +1,162 @@
+"""Spike-linear on the GPU against the oracle.
+
+Tolerance (north star): fp32 outputs within max-abs 1e-4 x max|ref|.  The CSR
+branch keeps the reference engine's summation order and is checked bit-exact
+(against the C restatement of csr_coalesced_kernel and against the reference
+engine itself); CSR indices and counts are always bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import spk_oracle as O
+from spikestack_lite_b200 import ops
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4  # max |y - ref| / max |ref|
+
+
+def _spikes(T, M, K, p, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.rand(T, M, K, generator=g, device="cuda") < p).float()
+
+
+def _weight(N, K, seed, dtype=torch.float32):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(N, K, generator=g, device="cuda") / K ** 0.5).to(dtype)
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+@pytest.mark.parametrize("T,M,K,N,p", [
+    (3, 257, 512, 128, 0.10),
+    (3, 16384, 512, 128, 0.10),   # the isolated spike-linear config, full size
+    (2, 300, 2048, 512, 0.5),     # the model's fc2 geometry at its density
+    (1, 1, 64, 16, 1.0),
+    (2, 129, 96, 48, 0.3),        # N tile of 48, partial row tile
+    (1, 200, 128, 300, 0.2),      # N not a multiple of 16
+])
+def test_spike_linear_vs_oracle(branch, T, M, K, N, p):
+    S = _spikes(T, M, K, p, seed=M + K)
+    W = _weight(N, K, seed=N)
+    Y = ops.spike_linear(S, weight=W, branch=branch)
+    ref = O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy())
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_bf16_weight_sweep_shape(branch):
+    # the density-sweep geometry (K = N = 2048, bf16 W, fp32 accumulate), row slice
+    S = _spikes(2, 512, 2048, 0.05, seed=1)
+    W = _weight(2048, 2048, seed=2, dtype=torch.bfloat16)
+    Y = ops.spike_linear(S, weightT=W.t(), branch=branch)
+    ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy())
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+
+
+def test_csr_branch_bit_exact_with_reference_order():
+    S = _spikes(2, 300, 512, 0.1, seed=4)
+    W = _weight(128, 512, seed=5)
+    Y = ops.spike_linear(S, weight=W, branch="csr").cpu().numpy()
+    Sn, WT = S.cpu().numpy(), W.t().contiguous().cpu().numpy()
+    for t in range(2):
+        _, rp, ci, vals = O.csr_plane(Sn[t])
+        np.testing.assert_array_equal(Y[t], O.spmm_csr_exact(rp, ci, vals, WT))
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_real_valued_negative_and_nan_inputs(branch):
+    g = torch.Generator(device="cuda").manual_seed(8)
+    S = torch.randn(2, 200, 256, generator=g, device="cuda")
+    S[0, 1, 2] = float("nan")
+    W = _weight(64, 256, seed=9)
+    Y = ops.spike_linear(S, weight=W, branch=branch)
+    ref = O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy())  # only S > 0 contributes
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_bias_and_golden(golden, branch):
+    z = golden("spike_linear")
+    S = torch.from_numpy(z["bin_x"]).cuda()
+    Y = ops.spike_linear(S, weight=torch.from_numpy(z["mod_w"]).cuda(), bias=torch.from_numpy(z["mod_b"]).cuda(),
+                         branch=branch)
+    assert O.rel_err(Y.cpu().numpy(), z["mod_y"]) < TOL
+    S2 = torch.from_numpy(z["real_x"]).cuda()
+    Y2 = ops.spike_linear(S2, weightT=torch.from_numpy(z["real_w"]).t().cuda(), branch=branch)
+    assert O.rel_err(Y2.cpu().numpy(), z["real_y"]) < TOL
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_csr_outputs_with_product(branch):
+    T, M, K = 3, 1000, 512
+    S = _spikes(T, M, K, 0.1, seed=11)
+    W = _weight(128, K, seed=12)
+    csr = ops.alloc_csr(T, M, K, "cuda", values=True)
+    Y = ops.spike_linear(S, weight=W, csr=csr, branch=branch)
+    exp = O.csr_planes(S.cpu().numpy())
+    n = int(exp[4][-1])
+    np.testing.assert_array_equal(csr["nnz_row"].cpu().numpy(), exp[0].reshape(-1))
+    np.testing.assert_array_equal(csr["row_ptr"].cpu().numpy(), exp[1].reshape(-1))
+    np.testing.assert_array_equal(csr["plane_ptr"].cpu().numpy(), exp[4])
+    np.testing.assert_array_equal(csr["col_idx"][:n].cpu().numpy(), exp[2])
+    np.testing.assert_array_equal(csr["values"][:n].cpu().numpy(), exp[3])
+    assert O.rel_err(Y.cpu().numpy(), O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy())) < TOL
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_reference_multistep_op_semantics(branch):
+    # raw engine op as the reference tests call it (test_sparse.py:128-144)
+    torch.manual_seed(11)
+    B, T, I, O_ = 257, 3, 2048, 128
+    x = torch.rand(T, B, I, device="cuda").round()
+    w = torch.randn(O_, I, device="cuda")
+    from spikestack_lite_b200.sparse import alloc_csr_buffers
+
+    nnz, roff, ci, vals = alloc_csr_buffers(B, I, device="cuda")
+    out = ops.sparse_multistep_forward(x, w.t().contiguous(), nnz, roff, ci, vals, T, branch=branch)
+    assert torch.allclose(out, x @ w.t(), atol=1e-3, rtol=1e-3)
+    exp = O.csr_plane(x[-1].cpu().numpy())  # the buffers hold plane T-1
+    n = int(exp[1][-1])
+    np.testing.assert_array_equal(nnz.cpu().numpy(), exp[0])
+    np.testing.assert_array_equal(roff.cpu().numpy(), exp[1])
+    np.testing.assert_array_equal(ci[:n].cpu().numpy(), exp[2])
+    np.testing.assert_array_equal(vals[:n].cpu().numpy(), exp[3])
+    out1 = ops.sparse_forward(x[0].contiguous(), w.t().contiguous(), nnz, roff, ci, vals, branch=branch)
+    assert torch.allclose(out[0], out1, atol=1e-3, rtol=1e-3)
+
+
+def test_reference_engine_parity(ref_engine):
+    """Against the reference's own CUDA engine on the same inputs: CSR of the
+    last plane bit-exact, Y bit-exact on the CSR branch."""
+    ref = ref_engine("spikeskip_ref")
+    torch.manual_seed(3)
+    T, B, I, O_ = 3, 1000, 512, 128
+    x = (torch.rand(T, B, I, device="cuda") < 0.1).float()
+    wT = (torch.randn(O_, I, device="cuda") / I ** 0.5).t().contiguous()
+    from spikestack_lite_b200.sparse import alloc_csr_buffers
+
+    bufs_r = alloc_csr_buffers(B, I, device="cuda")
+    bufs_o = alloc_csr_buffers(B, I, device="cuda")
+    y_r = ref.sparse_multistep_forward(x, wT, *bufs_r, T)
+    y_o = ops.sparse_multistep_forward(x, wT, *bufs_o, T, branch="csr")
+    n = int(bufs_r[1][-1].item())
+    for a, b in zip(bufs_o[:2], bufs_r[:2]):
+        torch.testing.assert_close(a, b, rtol=0, atol=0)
+    torch.testing.assert_close(bufs_o[2][:n], bufs_r[2][:n], rtol=0, atol=0)
+    torch.testing.assert_close(bufs_o[3][:n], bufs_r[3][:n], rtol=0, atol=0)
+    torch.testing.assert_close(y_o, y_r, rtol=0, atol=0)
+    y_d = ops.sparse_multistep_forward(x, wT, *bufs_o, T, branch="dense")
+    assert O.rel_err(y_d.cpu().numpy(), y_r.cpu().numpy()) < TOL
+
+
+def test_full_size_properties():
+    """Full isolated-config size: linearity in the weight and plane
+    independence (size-independent properties) on the dense branch."""
+    S = _spikes(3, 16384, 512, 0.1, seed=21)
+    W1, W2 = _weight(128, 512, seed=22), _weight(128, 512, seed=23)
+    Y1 = ops.spike_linear(S, weight=W1)
+    Y2 = ops.spike_linear(S, weight=W2)
+    Y12 = ops.spike_linear(S, weight=W1 + W2)
+    scale = Y12.abs().max().item()
+    assert (Y12 - Y1 - Y2).abs().max().item() / scale < 3e-5
+    Yp = ops.spike_linear(S[1:2].contiguous(), weight=W1)
+    torch.testing.assert_close(Yp[0], Y1[1], rtol=0, atol=0)
