@@ -196,6 +196,11 @@ def run_spike_linear(args, dist, cfg):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    if args.quick:  # eager steps only (the small case that ncu captures)
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+        return {"workload": cfg["name"], "quick": True, "steps": args.steps}
     launches0 = _lib.launch_count()
 
     # CUDA graphs (one per input set) keep the host out of the timed region
@@ -509,11 +514,16 @@ def main():
     ap.add_argument("--p", type=float, default=None, help="spike density override")
     ap.add_argument("--branch", default="dense", choices=["auto", "dense", "csr"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="eager steps only, no JSON metrics (profiling case)")
+    ap.add_argument("--rows", type=int, default=None, help="override M (rows per plane) of spike-linear workloads")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(WORKLOADS[args.workload])
     if args.p is not None:
         cfg["p"] = args.p
+    if args.rows is not None:
+        cfg["M"] = args.rows
+        cfg["name"] += f" (M overridden to {args.rows})"
     dist = Dist()
 
     if args.impl == "reference":
