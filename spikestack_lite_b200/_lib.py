@@ -31,6 +31,7 @@ SIGNATURES = {
     "spk_profile_end": (_I, [_c.POINTER(_c.c_double), _c.POINTER(_L)]),
     "spk_csr_workspace_bytes": (_Z, [_I, _L, _I]),
     "spk_csr_compact": (_I, [_P, _I, _L, _I, _P, _P, _P, _P, _P, _L, _P, _Z, _P]),
+    "spk_csr_compact_noalloc": (_I, [_P, _I, _L, _I, _P, _P, _P, _P, _P, _L, _P]),
     "spk_spike_linear_workspace_bytes": (_Z, [_I, _L, _I, _I, _I]),
     "spk_spike_linear": (_I, [_P, _I, _L, _I, _P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _L, _I, _P, _Z, _P]),
     "spk_sparse_forward_workspace_bytes": (_Z, [_I, _L, _I, _I]),

@@ -7,3 +7,4 @@
 #include "spike_linear.cu"
 #include "attention.cu"
 #include "gsmc.cu"
+#include "csr_noalloc.cu"

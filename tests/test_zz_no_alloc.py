@@ -1,0 +1,87 @@
+"""spk_csr_compact_noalloc, the compaction entry point for callers that cannot
+allocate device memory (hosts that own the device memory and give plugins no
+workspace; serving loops that forbid cudaMalloc after start-up).
+
+Called through the C ABI with ctypes, it must produce exactly what the
+workspace-taking spk_csr_compact produces on the same input -- the CSR is
+integer/index work, so the comparison is bit-exact -- on two calls in a row
+(the calls share the library's fixed scratch array), and it must refuse a
+problem larger than that array with an error instead of touching memory.
+This file is collected last and also passes when run alone in a fresh process.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from spikestack_lite_b200 import _lib, build
+
+    build.build()
+    return _lib.load()
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _buffers(T, M, K, cap, dev):
+    return {
+        "nnz_row": torch.full((T * M,), -1, dtype=torch.int32, device=dev),
+        "row_ptr": torch.full((T * (M + 1),), -1, dtype=torch.int32, device=dev),
+        "col_idx": torch.full((cap,), -1, dtype=torch.int32, device=dev),
+        "values": torch.full((cap,), -1.0, dtype=torch.float32, device=dev),
+        "plane_ptr": torch.full((T + 1,), -1, dtype=torch.int64, device=dev),
+    }
+
+
+def _run(lib, S, noalloc):
+    from spikestack_lite_b200._lib import check
+
+    T, M, K = S.shape
+    cap = int((S > 0).sum().item()) + 16
+    b = _buffers(T, M, K, cap, S.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(S.device).cuda_stream)
+    args = (_ptr(S), T, M, K, _ptr(b["nnz_row"]), _ptr(b["row_ptr"]), _ptr(b["col_idx"]), _ptr(b["values"]),
+            _ptr(b["plane_ptr"]), cap)
+    if noalloc:
+        check(lib.spk_csr_compact_noalloc(*args, stream), "spk_csr_compact_noalloc")
+    else:
+        ws = torch.empty(lib.spk_csr_workspace_bytes(T, M, K), dtype=torch.uint8, device=S.device)
+        check(lib.spk_csr_compact(*args, _ptr(ws), ws.numel(), stream), "spk_csr_compact")
+    torch.cuda.synchronize()
+    return {k: v.cpu().numpy() for k, v in b.items()}
+
+
+def test_noalloc_matches_workspace_entry_point_twice(lib):
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(123)
+    # two calls in a row on the shared scratch: different shapes and densities
+    for T, M, K, p in [(3, 16384, 512, 0.10), (2, 5000, 2048, 0.3)]:
+        S = (torch.rand(T, M, K, generator=g, device=dev) < p).float()
+        S[0, 0, :7] = torch.tensor([0.5, -1.0, float("nan"), 2.0, 0.0, 1.0, 3.5], device=dev)
+        want = _run(lib, S, noalloc=False)
+        got = _run(lib, S, noalloc=True)
+        for key in want:
+            np.testing.assert_array_equal(got[key], want[key], err_msg=f"{key} (T={T}, M={M}, K={K})")
+        assert got["plane_ptr"][-1] == int((S > 0).sum().item())
+
+
+def test_noalloc_rejects_problems_beyond_the_fixed_scratch(lib):
+    from spikestack_lite_b200._lib import SPK_EWORKSPACE
+
+    dev = torch.device("cuda", 0)
+    S = torch.zeros(1, 8, 64, device=dev)
+    one = torch.zeros(64, dtype=torch.int32, device=dev)
+    pp = torch.zeros(2, dtype=torch.int64, device=dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    # 64 planes x 2^18 rows of 64 columns = 131072 row tiles: above the 1 MiB array
+    rc = lib.spk_csr_compact_noalloc(_ptr(S), 64, 1 << 18, 64, None, _ptr(one), _ptr(one), None, _ptr(pp), 64,
+                                     stream)
+    assert rc == SPK_EWORKSPACE
+    assert b"fixed" in lib.spk_last_error()
