@@ -26,7 +26,8 @@ namespace spk {
 
 struct ScanState {
   unsigned int tile_counter;
-  unsigned int pad[63];
+  int nonunit;  // set by the dense kernel when it saw a positive value other than 1
+  unsigned int pad[62];
   // followed by: uint64_t tile_desc[num_tiles]; uint64_t plane_desc[T]; uint8_t tile_flags[num_tiles]
 };
 
@@ -78,6 +79,8 @@ struct CsrArgs {
   uint64_t* tile_desc;
   uint64_t* plane_desc;
   uint8_t* tile_flags;     // [num_tiles]: 1 if the tile holds a positive value != 1
+  const uint32_t* bitmap;  // bitmap source: [T*M][KW] packed spikes written by the dense kernel
+  const int32_t* row_cnt;  // bitmap source: [T*M] spikes per row
 };
 
 __device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
@@ -95,6 +98,9 @@ __device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
   }
 }
 
+// FROM_BITMAP: phase A copies the packed bitmap and the row counts the dense
+// kernel already produced (K/8 bytes per row instead of 4K bytes of S).
+template <bool FROM_BITMAP>
 __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
   extern __shared__ __align__(16) uint32_t smem_u32buf[];
   const int RT = a.rows_per_tile;
@@ -121,7 +127,14 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 
   // ---- phase A: ballot rows into the shared bitmap
   bool nonunit = false;
-  for (int r = warp; r < RT; r += 8) {
+  if (FROM_BITMAP) {
+    const int64_t grow0 = (int64_t)plane * a.M + row0;
+    const uint32_t* src = a.bitmap + grow0 * a.KW;
+    for (int64_t i = threadIdx.x; i < (int64_t)rows * a.KW; i += blockDim.x) bm[i] = src[i];
+    for (int r = threadIdx.x; r < RT; r += blockDim.x) cnt[r] = (r < rows) ? a.row_cnt[grow0 + r] : 0;
+    if (threadIdx.x == 0) s_nonunit = a.state->nonunit != 0;
+  }
+  for (int r = warp; r < RT && !FROM_BITMAP; r += 8) {
     int c = 0;
     if (r < rows) {
       const float* row = Sp + (int64_t)r * a.K;
@@ -219,7 +232,8 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
           const int64_t p = pos + __popc(bits & lt);
           if (p < a.col_capacity) {
             a.col_idx[p] = w * 32 + lane;
-            if (a.values) a.values[p] = row[w * 32 + lane];
+            // spikes of unit value need no gather from S
+            if (a.values) a.values[p] = (FROM_BITMAP && !s_nonunit) ? 1.0f : row[w * 32 + lane];
           } else {
             overflow = true;
           }
@@ -232,10 +246,14 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 
 }
 
-// Launch helper shared by every entry point that emits CSR.
-int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
-                    int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
-                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out) {
+// Launch helper shared by every entry point that emits CSR.  With `bitmap`
+// set, the scan reads the packed spikes and row counts of a preceding dense
+// pass instead of S (S is then only read for values of non-unit spikes), and
+// `state_zeroed` says that pass already cleared the scan state.
+int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* row_cnt, bool state_zeroed, int T,
+                       int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
+                       int64_t* plane_ptr, int64_t col_capacity, void* ws, cudaStream_t stream,
+                       const uint8_t** tile_flags_out, CsrLayout* layout_out) {
   const CsrLayout L = csr_layout(T, M, K);
   CsrArgs a{};
   a.S = S;
@@ -257,22 +275,32 @@ int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, i
   a.tile_desc = reinterpret_cast<uint64_t*>(base + L.desc_off);
   a.plane_desc = reinterpret_cast<uint64_t*>(base + L.plane_desc_off);
   a.tile_flags = reinterpret_cast<uint8_t*>(base + L.flags_off);
+  a.bitmap = bitmap;
+  a.row_cnt = row_cnt;
   const size_t smem = (size_t)L.rows_per_tile * L.KW * 4 + (size_t)L.rows_per_tile * 8;
+  auto kern = bitmap ? csr_scan_kernel<true> : csr_scan_kernel<false>;
   if (smem > 48 * 1024) {
-    SPK_CUDA_TRY(cudaFuncSetAttribute(csr_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
   // The tile counter and the look-back descriptors start from zero on every
   // launch (stream-ordered), so the workspace needs no persistent state and
   // can be shared with any other use between calls.
-  SPK_CUDA_TRY(cudaMemsetAsync(base, 0, L.flags_off, stream));
+  if (!state_zeroed) SPK_CUDA_TRY(cudaMemsetAsync(base, 0, L.flags_off, stream));
   prof_before(SPK_KERNEL_CSR_SCAN, stream);
-  csr_scan_kernel<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
+  kern<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
   prof_after(SPK_KERNEL_CSR_SCAN, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
   if (tile_flags_out) *tile_flags_out = a.tile_flags;
   if (layout_out) *layout_out = L;
   return SPK_OK;
+}
+
+int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
+                    int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
+                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out) {
+  return launch_csr_scan_ex(S, nullptr, nullptr, false, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
+                            col_capacity, ws, stream, tile_flags_out, layout_out);
 }
 
 int check_csr_shape(int T, int64_t M, int K) {

@@ -10,15 +10,11 @@
 
 namespace spk {
 
-// from csr.cu / spmm_csr.cu / spike_linear_tc.cu (single translation unit)
-struct CsrLayout;
-int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
-                    int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
-                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out);
-
 struct SlLayout {
-  size_t csr_state;     // look-back state for the scan (zero-initialised once)
+  size_t csr_state;     // look-back state of the CSR scan (cleared every call)
   size_t img;           // W image (dense branch)
+  size_t bitmap;        // packed spikes [T*M][ceil(K/32)] written by the dense kernel for the scan
+  size_t row_cnt;       // spikes per row [T*M]
   size_t csr_rowptr;    // internal CSR when the caller did not ask for it (CSR branch)
   size_t csr_planeptr;
   size_t csr_cols;
@@ -42,6 +38,10 @@ inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool inte
   off += align_up(csr_layout(T, M, K).total, 256);
   L.img = off;
   off += align_up(tc_plan(K, N, w_dtype).img_bytes, 1024);
+  L.bitmap = off;
+  off += align_up(sizeof(uint32_t) * (size_t)T * M * ((K + 31) / 32), 256);
+  L.row_cnt = off;
+  off += align_up(sizeof(int32_t) * (size_t)T * M, 256);
   if (internal_csr) {
     L.csr_rowptr = off;
     off += align_up(sizeof(int32_t) * (size_t)T * (M + 1), 256);
@@ -76,15 +76,27 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
   char* wsb = static_cast<char*>(ws);
 
   if (branch == SPK_BRANCH_DENSE) {
+    // w_image also clears the scan state (tile counter, look-back
+    // descriptors, non-unit flag); the dense kernel writes the packed spike
+    // bitmap and row counts; the scan expands them (no second read of S).
     const TcPlan p = tc_plan(K, N, w_dtype);
     unsigned char* img = reinterpret_cast<unsigned char*>(wsb + L.img);
-    rc = launch_w_image(W, w_dtype, sk, sn, K, N, p, img, stream);
+    const CsrLayout cl = csr_layout(T, M, K);
+    uint32_t* state = reinterpret_cast<uint32_t*>(wsb + L.csr_state);
+    rc = launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr,
+                        want_csr ? (int64_t)(cl.flags_off / 4) : 0, stream);
     if (rc) return rc;
-    rc = launch_tc(S, (int64_t)T * M, K, N, p, img, bias, Y, stream);
+    TcOut o{bias, Y, nullptr, nullptr, nullptr};
+    if (want_csr) {
+      o.bitmap = reinterpret_cast<uint32_t*>(wsb + L.bitmap);
+      o.row_cnt = reinterpret_cast<int32_t*>(wsb + L.row_cnt);
+      o.nonunit = reinterpret_cast<int*>(wsb + L.csr_state) + 1;  // ScanState::nonunit
+    }
+    rc = launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
     if (rc) return rc;
     if (want_csr) {
-      rc = launch_csr_scan(S, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr, col_capacity,
-                           wsb + L.csr_state, stream, nullptr, nullptr);
+      rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
+                              col_capacity, wsb + L.csr_state, stream, nullptr, nullptr);
     }
     return rc;
   }

@@ -1,101 +1,158 @@
 // Dense branch of spike-linear on the 5th-generation tensor cores.
 //
-// Y[r, n] = sum_k relu'(S[r, k]) * W[k, n] where relu'(x) = x if x > 0 else 0
-// (the reference engine's predicate, sparse_linear.cu:268), computed as a
-// K-major bf16 x bf16 -> fp32 tcgen05 contraction with the accumulator in
-// TMEM.  Spikes are exact in bf16; an fp32 operand is split into hi + lo bf16
-// halves so that the products keep ~2^-17 relative accuracy:
-//   W (fp32)  ->  W_hi + W_lo       (two MMAs per k-step)
-//   S (fp32)  ->  S_hi [+ S_lo]     (S_lo only for a k-chunk that holds a value
-//                                    not exact in bf16; spikes never need it)
+// Y[r, n] = sum_k relu'(S[r, k]) * W[k, n] (+ bias[n]), relu'(x) = x if x > 0
+// else 0 -- the reference engine's predicate (sparse_linear.cu:268) -- as a
+// K-major bf16 x bf16 -> fp32 tcgen05 contraction with TMEM accumulators.
+// Spikes are exact in bf16; fp32 operands are split into hi + lo bf16 halves
+// so that products keep ~2^-17 relative accuracy:
+//   W (fp32)  ->  W_hi + W_lo        two MMAs per k-step
+//   S (fp32)  ->  S_hi [+ S_lo]      S_lo only for a stage holding a value that
+//                                    bf16 does not represent (never for spikes)
 //
-// CTA = one 128-row x NT-column output tile, 10 warps:
-//   warps 0-3  producers: load S (fp32, 16 B per lane, coalesced), apply the
-//              predicate, convert to bf16 and store into the 128-byte-swizzled
-//              K-major A stage; per-warp flags tell the MMA issuer whether
-//              the stage needs the lo half;
-//   warp 8     allocates TMEM and streams the pre-split W image into the B
-//              stage with 1-D bulk copies (no multicast);
-//   warp 9     one thread issues tcgen05.mma and commits stage releases;
-//   warps 4-7  epilogue: tcgen05.ld of their 32-lane TMEM quarter, + bias,
-//              vectorised stores of Y.
-// All waits are bounded (2 s); a timeout raises SPK_DEV_PIPE_TIMEOUT, every
-// role drains what it issued, TMEM is freed and the kernel returns.
+// Work split: CTA (x, y) owns a contiguous range of rows (multiple of 32,
+// balanced over all SMs) for N-tile y.  Its rows are processed in groups of
+// G row tiles of 128; inside a group the K loop is outermost, so each weight
+// chunk is brought in once and used by all G tiles, whose accumulators sit
+// side by side in TMEM.  Two accumulator buffers let the epilogue of group g
+// overlap the MMAs of group g+1.
+//
+// Warp roles (320 threads):
+//   warp 0     TMA producer: S tiles via a 2-D tensor map (fp32, 32-row x
+//              64-column boxes, zero fill past the tensor edge) into a 3-slot
+//              staging ring; weight chunks of the pre-split image by 1-D bulk
+//              copy.  No multicast anywhere.
+//   warp 1     TMEM owner and MMA issuer (one thread).
+//   warps 2-5  converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
+//              128-byte-swizzled K-major A layout; optionally the packed spike
+//              bitmap and per-row counts the CSR pass consumes.
+//   warps 6-9  epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
+// Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; each role then
+// leaves its loop, issued copies and MMAs are drained, TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "spk_common.cuh"
 
 namespace spk {
 
 namespace tc {
 
-constexpr int kRows = 128;          // MMA M
-constexpr int kKChunk = 64;         // bf16 elements per 128-byte swizzle row
-constexpr int kABytes = kRows * 128;  // one A stage half (hi or lo): 16 KB
+constexpr int kRows = 128;              // MMA M: one row tile
+constexpr int kKChunk = 64;             // bf16 elements per 128-byte swizzle row
+constexpr int kABytes = kRows * 128;    // one A half (hi or lo) of a stage: 16 KB
+constexpr int kStgBytes = kRows * 256;  // fp32 staging of one stage: 32 KB
+constexpr int kBoxRows = 32;            // TMA box: 32 rows x 64 fp32 = 8 KB
+constexpr int kBoxBytes = kBoxRows * 256;
 constexpr int kThreads = 320;
+constexpr int kNS = 3;                  // staging slots
+constexpr int kNA = 2;                  // A slots (hi + lo each)
+constexpr int kNB = 2;                  // weight chunk slots
+
+__host__ __device__ constexpr int pow2_at_least(int x, int lo) {
+  int p = lo;
+  while (p < x) p <<= 1;
+  return p;
+}
 
 template <int NT, bool WSPLIT>
 struct Cfg {
+  static constexpr int kTileCols = ((NT + 31) / 32) * 32;          // TMEM columns per row tile
+  static constexpr int kG = (256 / kTileCols) > 4 ? 4 : (256 / kTileCols);  // row tiles per group
+  static constexpr int kAccCols = kG * kTileCols;                    // one accumulator buffer
+  static constexpr int kTmemCols = pow2_at_least(2 * kAccCols, 32);
   static constexpr int kBHalf = NT * 128;
   static constexpr int kBBytes = kBHalf * (WSPLIT ? 2 : 1);
-  static constexpr int kStageBytes = 2 * kABytes + kBBytes;
-  static constexpr int kStages = (200 * 1024) / kStageBytes >= 4 ? 4 : ((200 * 1024) / kStageBytes);
-  static constexpr int kTmemCols = NT <= 32 ? 32 : (NT <= 64 ? 64 : (NT <= 128 ? 128 : 256));
-  static constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-  static_assert(kStages >= 2, "stage ring too small");
+  static constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNA * 2 * kABytes + (size_t)kNB * kBBytes;
+  // barriers (2NS + 2NA + 2NB + 5 words), lo flags [NA][4], row counts [G][128], TMEM slot, abort flag
+  static constexpr size_t kTail = 8 * (2 * kNS + 2 * kNA + 2 * kNB + 5) + 16 * kNA + 4 * 128 * kG + 16;
+  static constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kRing + ((kTail + 255) / 256) * 256;
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "NT must be a multiple of 16 in [16, 256]");
+  static_assert(kTmemCols <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 }  // namespace tc
 
 struct TcArgs {
-  const float* S;
-  int64_t R;       // rows (T*M)
-  int K, N;
-  int nk;          // k-chunks of 64
-  const unsigned char* wimg;  // pre-split W image
+  int64_t R;              // rows (T*M)
+  int K, N, nk, KW;       // nk: 64-wide K chunks; KW: 32-bit bitmap words per row
+  const unsigned char* wimg;
   const float* bias;
   float* Y;
-  int y_vec;       // Y is 16-byte aligned and N % 4 == 0: float4 stores
+  int y_vec;              // Y 16-byte aligned and N % 4 == 0
+  int64_t rows_per_cta;   // multiple of 32
+  uint32_t* bitmap;       // [R][KW] packed spikes (bit k%32 of word k/32), or null
+  int32_t* row_cnt;       // [R] spikes per row, or null
+  int* nonunit;           // set to 1 when a positive value other than 1 is seen
 };
 
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
 template <int NT, bool WSPLIT>
-__global__ void __launch_bounds__(tc::kThreads, 1) spike_linear_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(tc::kThreads, 1)
+    spike_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
   using C = tc::Cfg<NT, WSPLIT>;
-  constexpr int ST = C::kStages;
+  constexpr int G = C::kG, NS = tc::kNS, NA = tc::kNA, NB = tc::kNB;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
-  // 1024-byte align the operand ring (required by the 128-byte swizzle)
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  unsigned char* a_hi = base;                          // [ST][16 KB]
-  unsigned char* a_lo = base + ST * tc::kABytes;       // [ST][16 KB]
-  unsigned char* bstg = base + 2 * ST * tc::kABytes;   // [ST][kBBytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bstg + (size_t)ST * C::kBBytes);
-  uint64_t* a_full = bars;            // [ST] 4 producer-warp arrivals
-  uint64_t* b_full = bars + ST;       // [ST] 1 arrival + tx bytes
-  uint64_t* empty = bars + 2 * ST;    // [ST] tcgen05.commit
-  uint64_t* acc_full = bars + 3 * ST; // [1]
-  uint64_t* drain = bars + 3 * ST + 1;
-  int* lo_flag = reinterpret_cast<int*>(bars + 3 * ST + 2);  // [ST][4 producer warps]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lo_flag + 4 * ST);
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  unsigned char* stg = base;                                     // [NS][32 KB] fp32 staging
+  unsigned char* a_hi = stg + NS * tc::kStgBytes;                // [NA][16 KB]
+  unsigned char* a_lo = a_hi + NA * tc::kABytes;                 // [NA][16 KB]
+  unsigned char* bst = a_lo + NA * tc::kABytes;                  // [NB][kBBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bst + (size_t)NB * C::kBBytes);
+  uint64_t* stg_full = bars;
+  uint64_t* stg_empty = stg_full + NS;
+  uint64_t* a_full = stg_empty + NS;
+  uint64_t* a_empty = a_full + NA;
+  uint64_t* b_full = a_empty + NA;
+  uint64_t* b_empty = b_full + NB;
+  uint64_t* acc_full = b_empty + NB;   // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* drain = acc_empty + 2;
+  int* lo_flag = reinterpret_cast<int*>(drain + 1);              // [NA][4]
+  int* row_count = lo_flag + NA * 4;                             // [G][128]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * tc::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r0 = (int64_t)blockIdx.x * tc::kRows;
+  const int64_t r_begin = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t r_end = min64(a.R, r_begin + a.rows_per_cta);
   const int n_tile = blockIdx.y;
   const int n0 = n_tile * NT;
   const int nk = a.nk;
+  const int tiles = r_end > r_begin ? (int)ceil_div(r_end - r_begin, tc::kRows) : 0;
+  const int groups = (tiles + G - 1) / G;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&stg_full[s], 1);
+      mbar_init(&stg_empty[s], 4);
+    }
+    for (int s = 0; s < NA; ++s) {
       mbar_init(&a_full[s], 4);
-      mbar_init(&b_full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&a_empty[s], 1);
       for (int w = 0; w < 4; ++w) lo_flag[4 * s + w] = 0;
     }
-    mbar_init(acc_full, 1);
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_empty[s], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -104,165 +161,248 @@ __global__ void __launch_bounds__(tc::kThreads, 1) spike_linear_tc_kernel(TcArgs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ------------------------------------------------------------ producers
-    // Each warp owns rows [32w, 32w+32) of the tile.  Its share of the lo
-    // stage is written only when it holds a value that is not exact in bf16;
-    // otherwise it is zero-filled once per ring slot ("dirty" tracks slots
-    // that may still hold nonzero lo data) so that a stage whose other warps
-    // need the lo MMA still sees zeros here.
-    const int half = lane >> 4;            // which of the 2 rows this lane loads
-    const int kq = (lane & 15) * 4;        // first of the 4 columns within the chunk
-    uint32_t dirty = (1u << ST) - 1u;      // ring slots whose lo share is not known to be zero
-    for (int kc = 0; kc < nk; ++kc) {
-      const int s = kc % ST, u = kc / ST;
-      if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) break;
-      const int k = kc * tc::kKChunk + kq;
-      float4 v[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int rl = warp * 32 + 2 * i + half;
-        const int64_t row = r0 + rl;
-        if (row < a.R && k < a.K) {
-          v[i] = __ldg(reinterpret_cast<const float4*>(a.S + row * a.K + k));
-        } else {
-          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      bool any_lo = false;
-      uint2 lo_pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int rl = warp * 32 + 2 * i + half;
-        float x[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-        __nv_bfloat16 h[4], l[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float xr = x[j] > 0.0f ? x[j] : 0.0f;
-          split_bf16(xr, h[j], l[j]);
-          any_lo |= (__bfloat16_as_ushort(l[j]) & 0x7fffu) != 0;
-        }
-        const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
-        *reinterpret_cast<uint2*>(a_hi + s * tc::kABytes + off) =
-            make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
-        lo_pk[i] = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
-      }
-      const bool warp_lo = __any_sync(0xffffffffu, any_lo);
-      if (warp_lo || ((dirty >> s) & 1u)) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int rl = warp * 32 + 2 * i + half;
-          const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
-          *reinterpret_cast<uint2*>(a_lo + s * tc::kABytes + off) = warp_lo ? lo_pk[i] : make_uint2(0u, 0u);
-        }
-        dirty = warp_lo ? (dirty | (1u << s)) : (dirty & ~(1u << s));
-      }
-      if (lane == 0) lo_flag[s * 4 + warp] = warp_lo ? 1 : 0;
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[s]);
-    }
-  } else if (warp == 8) {
-    // ------------------------------------------------------------ B loader
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int kc = 0; kc < nk; ++kc) {
-        const int s = kc % ST, u = kc / ST;
-        if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) break;
-        mbar_arrive_expect_tx(&b_full[s], C::kBBytes);
-        bulk_g2s(bstg + (size_t)s * C::kBBytes, a.wimg + ((size_t)n_tile * nk + kc) * C::kBBytes, C::kBBytes,
-                 &b_full[s]);
-        issued = kc + 1;
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_s)) : "memory");
+      int j = 0, jb = 0;
+      bool ok = true;
+      for (int g = 0; g < groups && ok; ++g) {
+        const int tg = min(G, tiles - g * G);
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          const int sb = jb % NB;
+          if (jb >= NB && !(ok = mbar_wait(&b_empty[sb], ((jb / NB) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
+            break;
+          mbar_arrive_expect_tx(&b_full[sb], C::kBBytes);
+          bulk_g2s(bst + (size_t)sb * C::kBBytes, a.wimg + ((size_t)n_tile * nk + kc) * C::kBBytes, C::kBBytes,
+                   &b_full[sb]);
+          ++jb;
+          for (int t = 0; t < tg; ++t) {
+            const int s = j % NS;
+            if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
+              break;
+            const int64_t row0 = r_begin + (int64_t)(g * G + t) * tc::kRows;
+            const int nrows = (int)min64(tc::kRows, r_end - row0);
+            const int nbox = (nrows + tc::kBoxRows - 1) / tc::kBoxRows;
+            mbar_arrive_expect_tx(&stg_full[s], nbox * tc::kBoxBytes);
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(stg + s * tc::kStgBytes + b * tc::kBoxBytes, &tmap_s, kc * tc::kKChunk,
+                          (int)(row0 + b * tc::kBoxRows), &stg_full[s]);
+            ++j;
+          }
+        }
       }
-      // drain: every issued copy must land before shared memory is released
-      for (int kc = (issued > ST ? issued - ST : 0); kc < issued; ++kc) {
-        mbar_wait(&b_full[kc % ST], (kc / ST) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
-      }
+      // every issued copy lands before the CTA can leave
+      for (int i = (j > NS ? j - NS : 0); i < j; ++i)
+        mbar_wait(&stg_full[i % NS], (i / NS) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
+      for (int i = (jb > NB ? jb - NB : 0); i < jb; ++i)
+        mbar_wait(&b_full[i % NB], (i / NB) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_f32(tc::kRows, NT);
+      int j = 0, jb = 0;
       bool ok = true;
-      for (int kc = 0; kc < nk && ok; ++kc) {
-        const int s = kc % ST, u = kc / ST;
-        ok = mbar_wait(&a_full[s], u & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT) &&
-             mbar_wait(&b_full[s], u & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT);
-        if (!ok) break;
+      for (int g = 0; g < groups && ok; ++g) {
+        const int tg = min(G, tiles - g * G);
+        const int ab = g & 1;
+        if (g >= 2 && !(ok = mbar_wait(&acc_empty[ab], ((g / 2) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         tc_fence_after();
-        const uint64_t da_hi = umma_desc_sw128_kmajor(smem_u32(a_hi + s * tc::kABytes));
-        const uint64_t da_lo = umma_desc_sw128_kmajor(smem_u32(a_lo + s * tc::kABytes));
-        const uint64_t db_hi = umma_desc_sw128_kmajor(smem_u32(bstg + (size_t)s * C::kBBytes));
-        const uint64_t db_lo = umma_desc_sw128_kmajor(smem_u32(bstg + (size_t)s * C::kBBytes + C::kBHalf));
-        const bool lo = (lo_flag[4 * s] | lo_flag[4 * s + 1] | lo_flag[4 * s + 2] | lo_flag[4 * s + 3]) != 0;
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          const int sb = jb % NB;
+          if (!(ok = mbar_wait(&b_full[sb], (jb / NB) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          const uint64_t db_hi = umma_desc_sw128_kmajor(smem_u32(bst + (size_t)sb * C::kBBytes));
+          const uint64_t db_lo = umma_desc_sw128_kmajor(smem_u32(bst + (size_t)sb * C::kBBytes + C::kBHalf));
+          for (int t = 0; t < tg; ++t) {
+            const int sa = j % NA;
+            if (!(ok = mbar_wait(&a_full[sa], (j / NA) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+            tc_fence_after();
+            const uint64_t da_hi = umma_desc_sw128_kmajor(smem_u32(a_hi + sa * tc::kABytes));
+            const uint64_t da_lo = umma_desc_sw128_kmajor(smem_u32(a_lo + sa * tc::kABytes));
+            const bool lo = (lo_flag[4 * sa] | lo_flag[4 * sa + 1] | lo_flag[4 * sa + 2] | lo_flag[4 * sa + 3]) != 0;
+            const uint32_t d = tmem + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
 #pragma unroll
-        for (int j = 0; j < tc::kKChunk / 16; ++j) {
-          const uint64_t adv = (uint64_t)(2 * j);  // 32 bytes per 16-element k-step
-          umma_f16_ss(tmem, da_hi + adv, db_hi + adv, idesc, (kc > 0 || j > 0) ? 1u : 0u);
-          if (WSPLIT) umma_f16_ss(tmem, da_hi + adv, db_lo + adv, idesc, 1u);
-          if (lo) umma_f16_ss(tmem, da_lo + adv, db_hi + adv, idesc, 1u);
+            for (int kk = 0; kk < tc::kKChunk / 16; ++kk) {
+              const uint64_t adv = (uint64_t)(2 * kk);  // 32 bytes per 16-element k-step
+              umma_f16_ss(d, da_hi + adv, db_hi + adv, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+              if (WSPLIT) umma_f16_ss(d, da_hi + adv, db_lo + adv, idesc, 1u);
+              if (lo) umma_f16_ss(d, da_lo + adv, db_hi + adv, idesc, 1u);
+            }
+            umma_commit(&a_empty[sa]);
+            ++j;
+          }
+          if (!ok) break;
+          umma_commit(&b_empty[sb]);
+          ++jb;
         }
-        umma_commit(&empty[s]);
+        if (ok) umma_commit(&acc_full[ab]);
       }
-      umma_commit(ok ? acc_full : drain);
-      if (!ok) mbar_wait(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);  // issued MMAs finish before exit
+      if (!ok) {  // issued MMAs finish before TMEM and shared memory are released
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- converters
+    // Warp cw owns rows [32cw, 32cw+32) of each tile; in load i a lane holds
+    // 4 columns of row 32cw + 2i + (lane >> 4).  The lo share of an A slot is
+    // written only when this warp holds a value bf16 does not represent, and
+    // zero-filled once otherwise ("dirty" tracks slots that may hold nonzero
+    // lo data), so a slot whose other warps need the lo MMA sees zeros here.
+    const int cw = warp - 2;
+    const int half = lane >> 4;
+    const int kq = (lane & 15) * 4;
+    const bool emit = (a.bitmap != nullptr) && n_tile == 0;
+    uint32_t dirty = (1u << NA) - 1u;
+    int j = 0;
+    bool ok = true;
+    for (int g = 0; g < groups && ok; ++g) {
+      const int tg = min(G, tiles - g * G);
+      for (int kc = 0; kc < nk && ok; ++kc) {
+        for (int t = 0; t < tg; ++t) {
+          const int s = j % NS, sa = j % NA;
+          if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          if (j >= NA && !(ok = mbar_wait(&a_empty[sa], ((j / NA) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          const int64_t row0 = r_begin + (int64_t)(g * G + t) * tc::kRows;
+          const int nrows = (int)min64(tc::kRows, r_end - row0);
+          float4 v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int rl = cw * 32 + 2 * i + half;
+            v[i] = (rl < nrows) ? *reinterpret_cast<const float4*>(stg + s * tc::kStgBytes + rl * 256 + kq * 4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&stg_empty[s]);  // the staging slot is free once all 4 warps hold their data
+          bool any_lo = false, nonunit = false;
+          uint2 lo_pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int rl = cw * 32 + 2 * i + half;
+            const float x[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+            __nv_bfloat16 h[4], l[4];
+            uint32_t nib = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const bool nz = x[e] > 0.0f;
+              nib |= (nz ? 1u : 0u) << e;
+              nonunit |= nz && (x[e] != 1.0f);
+              split_bf16(nz ? x[e] : 0.0f, h[e], l[e]);
+              any_lo |= (__bfloat16_as_ushort(l[e]) & 0x7fffu) != 0;
+            }
+            const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
+            *reinterpret_cast<uint2*>(a_hi + sa * tc::kABytes + off) =
+                make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+            lo_pk[i] = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+            if (emit) {
+              // 32-column words: lanes 16h..16h+7 hold columns 0-31 of the chunk, 16h+8.. columns 32-63
+              uint32_t w = nib << (4 * (lane & 7));
+              w |= __shfl_xor_sync(0xffffffffu, w, 1);
+              w |= __shfl_xor_sync(0xffffffffu, w, 2);
+              w |= __shfl_xor_sync(0xffffffffu, w, 4);
+              const uint32_t w_hi = __shfl_down_sync(0xffffffffu, w, 8);
+              if ((lane & 15) == 0 && rl < nrows) {
+                const int64_t grow = row0 + rl;
+                const int idx = t * tc::kRows + rl;
+                const int c = __popc(w) + (kc * 2 + 1 < a.KW ? __popc(w_hi) : 0);
+                row_count[idx] = (kc == 0 ? 0 : row_count[idx]) + c;
+                uint32_t* bw = a.bitmap + grow * a.KW + kc * 2;
+                if (kc * 2 + 1 < a.KW && ((reinterpret_cast<uintptr_t>(bw) & 7) == 0)) {
+                  *reinterpret_cast<uint2*>(bw) = make_uint2(w, w_hi);
+                } else {
+                  bw[0] = w;
+                  if (kc * 2 + 1 < a.KW) bw[1] = w_hi;
+                }
+                if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = row_count[idx];
+              }
+            }
+          }
+          const bool warp_lo = __any_sync(0xffffffffu, any_lo);
+          if (warp_lo || ((dirty >> sa) & 1u)) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int rl = cw * 32 + 2 * i + half;
+              const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
+              *reinterpret_cast<uint2*>(a_lo + sa * tc::kABytes + off) = warp_lo ? lo_pk[i] : make_uint2(0u, 0u);
+            }
+            dirty = warp_lo ? (dirty | (1u << sa)) : (dirty & ~(1u << sa));
+          }
+          if (emit && a.nonunit && __any_sync(0xffffffffu, nonunit) && lane == 0) atomicOr(a.nonunit, 1);
+          if (lane == 0) lo_flag[sa * 4 + cw] = warp_lo ? 1 : 0;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[sa]);
+          ++j;
+        }
+      }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 4-7)
-    const int q = warp & 3;
-    const bool ok = mbar_wait(acc_full, 0, abort_flag, SPK_DEV_PIPE_TIMEOUT);
-    tc_fence_after();
-    if (ok) {
-      const int64_t row = r0 + q * 32 + lane;
-      const bool vec_ok = a.y_vec != 0;
+    // ---------------------------------------------------------------- epilogue (warps 6-9)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    for (int g = 0; g < groups; ++g) {
+      const int tg = min(G, tiles - g * G);
+      const int ab = g & 1;
+      if (!mbar_wait(&acc_full[ab], (g / 2) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) break;
+      tc_fence_after();
+      for (int t = 0; t < tg; ++t) {
+        const int64_t row = r_begin + (int64_t)(g * G + t) * tc::kRows + q * 32 + lane;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
 #pragma unroll 1
-      for (int c = 0; c < NT / 16; ++c) {
-        float acc[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 16), acc);
-        tmem_wait_ld();
-        const int n = n0 + c * 16;
-        if (row < a.R) {
-          float* y = a.Y + row * a.N + n;
-          if (vec_ok && n + 16 <= a.N) {
+        for (int c = 0; c < NT / 16; ++c) {
+          float acc[16];
+          tmem_ld16(tbase + (uint32_t)(c * 16), acc);
+          tmem_wait_ld();
+          const int n = n0 + c * 16;
+          if (row < r_end) {
+            float* y = a.Y + row * a.N + n;
+            if (a.y_vec && n + 16 <= a.N) {
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              float4 o = make_float4(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3]);
-              if (a.bias) {
-                o.x += a.bias[n + 4 * g];
-                o.y += a.bias[n + 4 * g + 1];
-                o.z += a.bias[n + 4 * g + 2];
-                o.w += a.bias[n + 4 * g + 3];
+              for (int gq = 0; gq < 4; ++gq) {
+                float4 o = make_float4(acc[4 * gq], acc[4 * gq + 1], acc[4 * gq + 2], acc[4 * gq + 3]);
+                if (a.bias) {
+                  o.x += a.bias[n + 4 * gq];
+                  o.y += a.bias[n + 4 * gq + 1];
+                  o.z += a.bias[n + 4 * gq + 2];
+                  o.w += a.bias[n + 4 * gq + 3];
+                }
+                *reinterpret_cast<float4*>(y + 4 * gq) = o;
               }
-              *reinterpret_cast<float4*>(y + 4 * g) = o;
-            }
-          } else {
+            } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (n + j < a.N) y[j] = a.bias ? acc[j] + a.bias[n + j] : acc[j];
+              for (int e = 0; e < 16; ++e)
+                if (n + e < a.N) y[e] = a.bias ? acc[e] + a.bias[n + e] : acc[e];
             }
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
-    tc_fence_before();
   }
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
-// Pre-split weight image: for n-tile t and k-chunk c, an [NT x 64] bf16 hi
+// Pre-split weight image: for N-tile t and K-chunk c, an [NT x 64] bf16 hi
 // block followed (fp32 W) by the lo block, each in the 128-byte-swizzled
-// K-major layout the B operand uses, so one bulk copy moves a whole stage.
+// K-major layout of the B operand, so one bulk copy moves a whole chunk.
+// The first thread also clears `zero_words` 32-bit words at `zero` (the CSR
+// scan state and the non-unit flag of the same call), saving a memset node.
 template <typename WT, bool WSPLIT>
-__global__ void w_image_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk,
-                               unsigned char* img) {
+__global__ void w_image_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk, unsigned char* img,
+                               uint32_t* zero, int64_t zero_words) {
   const int64_t total = (int64_t)((N + NT - 1) / NT) * NT * nk * 8;  // one thread per (n, 8 k)
   const size_t half = (size_t)NT * 128;
   const size_t stage = half * (WSPLIT ? 2 : 1);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < zero_words; i += nthr) zero[i] = 0u;
+  for (int64_t i = tid; i < total; i += nthr) {
     const int k8 = (int)(i % 8);
     const int64_t rest = i / 8;
     const int kc = (int)(rest % nk);
@@ -270,14 +410,14 @@ __global__ void w_image_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N
     const int t = (int)(ng / NT), nl = (int)(ng % NT);
     __nv_bfloat16 h[8], l[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int k = kc * 64 + k8 * 8 + j;
+    for (int e = 0; e < 8; ++e) {
+      const int k = kc * 64 + k8 * 8 + e;
       float x = 0.0f;
       if (k < K && ng < N) x = static_cast<float>(W[(int64_t)k * sk + ng * sn]);
       if (WSPLIT) {
-        split_bf16(x, h[j], l[j]);
+        split_bf16(x, h[e], l[e]);
       } else {
-        h[j] = __float2bfloat16_rn(x);
+        h[e] = __float2bfloat16_rn(x);
       }
     }
     unsigned char* blk = img + ((size_t)t * nk + kc) * stage;
@@ -315,15 +455,55 @@ inline bool tc_supported(int K, int N, const void* S) {
   return K >= 1 && N >= 1 && (K % 4) == 0 && (reinterpret_cast<uintptr_t>(S) % 16) == 0;
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// S [R, K] fp32 as a 2-D tensor: boxes of 64 columns x 32 rows, zero fill
+// outside the tensor (partial row tiles and K not a multiple of 64).
+static int make_s_map(CUtensorMap* map, const float* S, int64_t R, int K) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(SPK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)R};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)tc::kKChunk, (cuuint32_t)tc::kBoxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(S), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPK_ECUDA, "cuTensorMapEncodeTiled failed (%d) for S [%lld, %d]", (int)r,
+                                     (long long)R, K);
+  return SPK_OK;
+}
+
+struct TcOut {
+  const float* bias;
+  float* Y;
+  uint32_t* bitmap;
+  int32_t* row_cnt;
+  int* nonunit;
+};
+
 template <int NT, bool WSPLIT>
-int launch_tc_inst(const TcArgs& a, int n_tiles, cudaStream_t stream) {
+int launch_tc_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t stream) {
   using C = tc::Cfg<NT, WSPLIT>;
   auto kern = spike_linear_tc_kernel<NT, WSPLIT>;
   SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmemBytes));
-  dim3 grid((unsigned)ceil_div(a.R, tc::kRows), (unsigned)n_tiles);
-  SPK_REQUIRE(grid.x <= 2147483647u, "too many rows");
+  const int sms = sm_count();
+  const int ranges = sms / n_tiles > 0 ? sms / n_tiles : 1;
+  a.rows_per_cta = ceil_div(ceil_div(a.R, ranges), 32) * 32;
+  const int64_t gx = ceil_div(a.R, a.rows_per_cta);
+  dim3 grid((unsigned)gx, (unsigned)n_tiles);
   prof_before(SPK_KERNEL_DENSE, stream);
-  kern<<<grid, tc::kThreads, C::kSmemBytes, stream>>>(a);
+  kern<<<grid, tc::kThreads, C::kSmemBytes, stream>>>(map, a);
   prof_after(SPK_KERNEL_DENSE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
@@ -331,43 +511,59 @@ int launch_tc_inst(const TcArgs& a, int n_tiles, cudaStream_t stream) {
 }
 
 int launch_w_image(const void* W, int w_dtype, int64_t sk, int64_t sn, int K, int N, const TcPlan& p,
-                   unsigned char* img, cudaStream_t stream) {
+                   unsigned char* img, uint32_t* zero, int64_t zero_words, cudaStream_t stream) {
   const int64_t total = (int64_t)p.n_tiles * p.NT * p.nk * 8;
   const int threads = 256;
-  const int blocks = (int)min64(ceil_div(total, threads), 4096);
+  const int blocks = (int)min64(ceil_div(max64(total, zero_words), threads), 4096);
+  prof_before(SPK_KERNEL_W_IMAGE, stream);
   if (w_dtype == SPK_BF16) {
     w_image_kernel<__nv_bfloat16, false><<<blocks, threads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(W), sk, sn, K, N, p.NT, p.nk, img);
+        static_cast<const __nv_bfloat16*>(W), sk, sn, K, N, p.NT, p.nk, img, zero, zero_words);
   } else {
     w_image_kernel<float, true><<<blocks, threads, 0, stream>>>(static_cast<const float*>(W), sk, sn, K, N, p.NT,
-                                                               p.nk, img);
+                                                               p.nk, img, zero, zero_words);
   }
+  prof_after(SPK_KERNEL_W_IMAGE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
   return SPK_OK;
 }
 
-int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img,
-              const float* bias, float* Y, cudaStream_t stream) {
-  const int y_vec = ((N & 3) == 0 && (reinterpret_cast<uintptr_t>(Y) & 15) == 0) ? 1 : 0;
-  TcArgs a{S, R, K, N, p.nk, img, bias, Y, y_vec};
+int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
+              cudaStream_t stream) {
+  CUtensorMap map;
+  int rc = make_s_map(&map, S, R, K);
+  if (rc) return rc;
+  TcArgs a{};
+  a.R = R;
+  a.K = K;
+  a.N = N;
+  a.nk = p.nk;
+  a.KW = (K + 31) / 32;
+  a.wimg = img;
+  a.bias = o.bias;
+  a.Y = o.Y;
+  a.y_vec = ((N & 3) == 0 && (reinterpret_cast<uintptr_t>(o.Y) & 15) == 0) ? 1 : 0;
+  a.bitmap = o.bitmap;
+  a.row_cnt = o.row_cnt;
+  a.nonunit = o.nonunit;
   if (p.split) {
     switch (p.NT) {
-      case 16: return launch_tc_inst<16, true>(a, p.n_tiles, stream);
-      case 32: return launch_tc_inst<32, true>(a, p.n_tiles, stream);
-      case 48: return launch_tc_inst<48, true>(a, p.n_tiles, stream);
-      case 64: return launch_tc_inst<64, true>(a, p.n_tiles, stream);
-      case 128: return launch_tc_inst<128, true>(a, p.n_tiles, stream);
+      case 16: return launch_tc_inst<16, true>(map, a, p.n_tiles, stream);
+      case 32: return launch_tc_inst<32, true>(map, a, p.n_tiles, stream);
+      case 48: return launch_tc_inst<48, true>(map, a, p.n_tiles, stream);
+      case 64: return launch_tc_inst<64, true>(map, a, p.n_tiles, stream);
+      case 128: return launch_tc_inst<128, true>(map, a, p.n_tiles, stream);
       default: break;
     }
   } else {
     switch (p.NT) {
-      case 16: return launch_tc_inst<16, false>(a, p.n_tiles, stream);
-      case 32: return launch_tc_inst<32, false>(a, p.n_tiles, stream);
-      case 48: return launch_tc_inst<48, false>(a, p.n_tiles, stream);
-      case 64: return launch_tc_inst<64, false>(a, p.n_tiles, stream);
-      case 128: return launch_tc_inst<128, false>(a, p.n_tiles, stream);
-      case 256: return launch_tc_inst<256, false>(a, p.n_tiles, stream);
+      case 16: return launch_tc_inst<16, false>(map, a, p.n_tiles, stream);
+      case 32: return launch_tc_inst<32, false>(map, a, p.n_tiles, stream);
+      case 48: return launch_tc_inst<48, false>(map, a, p.n_tiles, stream);
+      case 64: return launch_tc_inst<64, false>(map, a, p.n_tiles, stream);
+      case 128: return launch_tc_inst<128, false>(map, a, p.n_tiles, stream);
+      case 256: return launch_tc_inst<256, false>(map, a, p.n_tiles, stream);
       default: break;
     }
   }

@@ -103,6 +103,36 @@ def test_csr_outputs_with_product(branch):
 
 
 @pytest.mark.parametrize("branch", ["dense", "csr"])
+def test_csr_outputs_real_valued(branch):
+    # values other than 1 must be gathered from S (the dense pass flags them)
+    g = torch.Generator(device="cuda").manual_seed(13)
+    T, M, K = 2, 700, 200
+    S = torch.randn(T, M, K, generator=g, device="cuda")
+    W = _weight(96, K, seed=14)
+    csr = ops.alloc_csr(T, M, K, "cuda", values=True)
+    Y = ops.spike_linear(S, weight=W, csr=csr, branch=branch)
+    exp = O.csr_planes(S.cpu().numpy())
+    n = int(exp[4][-1])
+    np.testing.assert_array_equal(csr["row_ptr"].cpu().numpy(), exp[1].reshape(-1))
+    np.testing.assert_array_equal(csr["col_idx"][:n].cpu().numpy(), exp[2])
+    np.testing.assert_array_equal(csr["values"][:n].cpu().numpy(), exp[3])
+    assert O.rel_err(Y.cpu().numpy(), O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy())) < TOL
+
+
+@pytest.mark.parametrize("rows", [1, 31, 33, 129, 4000, 50001])
+def test_dense_row_partition_edges(rows):
+    # row ranges are split over the SMs in multiples of 32 rows; tiles and boxes at the edges
+    S = _spikes(1, rows, 512, 0.1, seed=rows)
+    W = _weight(128, 512, seed=3)
+    csr = ops.alloc_csr(1, rows, 512, "cuda")
+    Y = ops.spike_linear(S, weight=W, csr=csr, branch="dense")
+    assert O.rel_err(Y.cpu().numpy(), O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy())) < TOL
+    exp = O.csr_planes(S.cpu().numpy())
+    np.testing.assert_array_equal(csr["row_ptr"].cpu().numpy(), exp[1].reshape(-1))
+    np.testing.assert_array_equal(csr["col_idx"][:int(exp[4][-1])].cpu().numpy(), exp[2])
+
+
+@pytest.mark.parametrize("branch", ["dense", "csr"])
 def test_reference_multistep_op_semantics(branch):
     # raw engine op as the reference tests call it (test_sparse.py:128-144)
     torch.manual_seed(11)
