@@ -177,21 +177,29 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
       if (r < RT) pre[r] = (int)running + incl - v;
       running += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0 && valid_tile) {
-      const int64_t agg = running;
-      bool ok = true;
-      int64_t excl = 0;
-      if (tile == 0) {
-        st_relaxed_u64(&a.tile_desc[0], kDescIncl | (uint64_t)agg);
-      } else {
-        st_relaxed_u64(&a.tile_desc[tile], kDescAgg | (uint64_t)agg);
-        for (int64_t j = tile - 1; j >= 0 && ok; --j) {
-          const uint64_t d = spin_desc(&a.tile_desc[j], ok);
-          excl += (int64_t)(d & kDescValueMask);
-          if ((d >> 62) == 2) break;
-        }
-        st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
+    const int64_t agg = running;
+    bool ok = true;
+    int64_t excl = 0;
+    if (valid_tile && tile > 0) {
+      // warp-wide look-back: lane l probes tile j - l, 32 predecessors per
+      // round; the nearest inclusive prefix ends the walk.
+      if (lane == 0) st_relaxed_u64(&a.tile_desc[tile], kDescAgg | (uint64_t)agg);
+      __syncwarp();
+      for (int64_t j = tile - 1;; j -= 32) {
+        const int64_t idx = j - lane;
+        const uint64_t d = (idx >= 0) ? spin_desc(&a.tile_desc[idx], ok) : kDescIncl;  // before tile 0: prefix 0
+        const uint32_t incl = __ballot_sync(0xffffffffu, (d >> 62) == 2);
+        const int last = incl ? __ffs(incl) - 1 : 31;  // lanes 0..last contribute
+        int64_t v = (lane <= last) ? (int64_t)(d & kDescValueMask) : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        excl += v;
+        if (incl) break;
       }
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (lane == 0 && valid_tile) {
+      st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
       int64_t base;
       if (tip == 0) {
         base = excl;
@@ -219,26 +227,39 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
       rp[r] = (int32_t)(rel + pre[r] + cnt[r]);
       if (nr) nr[r] = cnt[r];
     }
-    const uint32_t lt = (1u << lane) - 1u;
+    // Expansion: lane l takes word w0 + l of the row, a warp scan of the word
+    // popcounts gives each lane its output offset, and the lane writes its
+    // word's columns in ascending order.
     bool overflow = false;
+    const bool unit_values = FROM_BITMAP && !s_nonunit;  // spikes of value 1 need no gather from S
     for (int r = warp; r < rows; r += 8) {
       int64_t pos = excl + pre[r];
       const uint32_t* bw = bm + r * a.KW;
       const float* row = Sp + (int64_t)r * a.K;
-      for (int w = 0; w < a.KW; ++w) {
-        const uint32_t bits = bw[w];
-        if (bits == 0u) continue;
-        if ((bits >> lane) & 1u) {
-          const int64_t p = pos + __popc(bits & lt);
+      for (int w0 = 0; w0 < a.KW; w0 += 32) {
+        const int w = w0 + lane;
+        uint32_t bits = (w < a.KW) ? bw[w] : 0u;
+        const int c = __popc(bits);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        int64_t p = pos + (incl - c);
+        while (bits) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1u;
+          const int col = w * 32 + b;
           if (p < a.col_capacity) {
-            a.col_idx[p] = w * 32 + lane;
-            // spikes of unit value need no gather from S
-            if (a.values) a.values[p] = (FROM_BITMAP && !s_nonunit) ? 1.0f : row[w * 32 + lane];
+            a.col_idx[p] = col;
+            if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
           } else {
             overflow = true;
           }
+          ++p;
         }
-        pos += __popc(bits);
+        pos += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
     if (__any_sync(0xffffffffu, overflow) && lane == 0) report_device_error(SPK_DEV_CSR_OVERFLOW);

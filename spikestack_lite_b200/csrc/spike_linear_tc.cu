@@ -16,16 +16,16 @@
 // side by side in TMEM.  Two accumulator buffers let the epilogue of group g
 // overlap the MMAs of group g+1.
 //
-// Warp roles (320 threads):
+// Warp roles (448 threads):
 //   warp 0     TMA producer: S tiles via a 2-D tensor map (fp32, 32-row x
 //              64-column boxes, zero fill past the tensor edge) into a 3-slot
 //              staging ring; weight chunks of the pre-split image by 1-D bulk
 //              copy.  No multicast anywhere.
 //   warp 1     TMEM owner and MMA issuer (one thread).
-//   warps 2-5  converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
+//   warps 2-9  converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
 //              128-byte-swizzled K-major A layout; optionally the packed spike
 //              bitmap and per-row counts the CSR pass consumes.
-//   warps 6-9  epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
+//   warps 10-13 epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; each role then
 // leaves its loop, issued copies and MMAs are drained, TMEM is freed.
 #include <cuda.h>
@@ -43,7 +43,8 @@ constexpr int kABytes = kRows * 128;    // one A half (hi or lo) of a stage: 16 
 constexpr int kStgBytes = kRows * 256;  // fp32 staging of one stage: 32 KB
 constexpr int kBoxRows = 32;            // TMA box: 32 rows x 64 fp32 = 8 KB
 constexpr int kBoxBytes = kBoxRows * 256;
-constexpr int kThreads = 320;
+constexpr int kConvWarps = 8;           // converter warps
+constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 constexpr int kNS = 3;                  // staging slots
 constexpr int kNA = 2;                  // A slots (hi + lo each)
 constexpr int kNB = 2;                  // weight chunk slots
@@ -64,7 +65,7 @@ struct Cfg {
   static constexpr int kBBytes = kBHalf * (WSPLIT ? 2 : 1);
   static constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNA * 2 * kABytes + (size_t)kNB * kBBytes;
   // barriers (2NS + 2NA + 2NB + 5 words), lo flags [NA][4], row counts [G][128], TMEM slot, abort flag
-  static constexpr size_t kTail = 8 * (2 * kNS + 2 * kNA + 2 * kNB + 5) + 16 * kNA + 4 * 128 * kG + 16;
+  static constexpr size_t kTail = 8 * (2 * kNS + 2 * kNA + 2 * kNB + 5) + 4 * kConvWarps * kNA + 4 * 128 * kG + 16;
   static constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kRing + ((kTail + 255) / 256) * 256;
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "NT must be a multiple of 16 in [16, 256]");
   static_assert(kTmemCols <= 512, "TMEM budget");
@@ -116,8 +117,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint64_t* acc_full = b_empty + NB;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint64_t* drain = acc_empty + 2;
-  int* lo_flag = reinterpret_cast<int*>(drain + 1);              // [NA][4]
-  int* row_count = lo_flag + NA * 4;                             // [G][128]
+  int* lo_flag = reinterpret_cast<int*>(drain + 1);              // [NA][kConvWarps]
+  int* row_count = lo_flag + NA * tc::kConvWarps;               // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * tc::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -133,12 +134,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&stg_full[s], 1);
-      mbar_init(&stg_empty[s], 4);
+      mbar_init(&stg_empty[s], tc::kConvWarps);
     }
     for (int s = 0; s < NA; ++s) {
-      mbar_init(&a_full[s], 4);
+      mbar_init(&a_full[s], tc::kConvWarps);
       mbar_init(&a_empty[s], 1);
-      for (int w = 0; w < 4; ++w) lo_flag[4 * s + w] = 0;
+      for (int w = 0; w < tc::kConvWarps; ++w) lo_flag[tc::kConvWarps * s + w] = 0;
     }
     for (int s = 0; s < NB; ++s) {
       mbar_init(&b_full[s], 1);
@@ -220,7 +221,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             tc_fence_after();
             const uint64_t da_hi = umma_desc_sw128_kmajor(smem_u32(a_hi + sa * tc::kABytes));
             const uint64_t da_lo = umma_desc_sw128_kmajor(smem_u32(a_lo + sa * tc::kABytes));
-            const bool lo = (lo_flag[4 * sa] | lo_flag[4 * sa + 1] | lo_flag[4 * sa + 2] | lo_flag[4 * sa + 3]) != 0;
+            int lo_any = 0;
+#pragma unroll
+            for (int w = 0; w < tc::kConvWarps; ++w) lo_any |= lo_flag[tc::kConvWarps * sa + w];
+            const bool lo = lo_any != 0;
             const uint32_t d = tmem + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
 #pragma unroll
             for (int kk = 0; kk < tc::kKChunk / 16; ++kk) {
@@ -243,17 +247,21 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         mbar_wait(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + tc::kConvWarps) {
     // ---------------------------------------------------------------- converters
-    // Warp cw owns rows [32cw, 32cw+32) of each tile; in load i a lane holds
-    // 4 columns of row 32cw + 2i + (lane >> 4).  The lo share of an A slot is
-    // written only when this warp holds a value bf16 does not represent, and
-    // zero-filled once otherwise ("dirty" tracks slots that may hold nonzero
-    // lo data), so a slot whose other warps need the lo MMA sees zeros here.
+    // Warp cw owns rows [16cw, 16cw+16) of each tile; in load i a lane holds
+    // 4 columns of row 16cw + 2i + (lane >> 4).  Fast path: the upper halves
+    // of the fp32 bits (exact for non-negative values with zero low halves,
+    // e.g. spikes) plus a bit test.  Only a warp holding another value (needs
+    // the predicate, rounding or a lo half) takes the exact hi/lo split; the
+    // lo share of an A slot is written then, and zero-filled once otherwise
+    // ("dirty" tracks slots that may hold nonzero lo data), so a slot whose
+    // other warps need the lo MMA sees zeros here.
     const int cw = warp - 2;
     const int half = lane >> 4;
     const int kq = (lane & 15) * 4;
     const bool emit = (a.bitmap != nullptr) && n_tile == 0;
+    const bool check_unit = emit && a.nonunit != nullptr;
     uint32_t dirty = (1u << NA) - 1u;
     int j = 0;
     bool ok = true;
@@ -266,37 +274,41 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           if (j >= NA && !(ok = mbar_wait(&a_empty[sa], ((j / NA) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
           const int64_t row0 = r_begin + (int64_t)(g * G + t) * tc::kRows;
           const int nrows = (int)min64(tc::kRows, r_end - row0);
-          float4 v[16];
+          constexpr int RPW = tc::kRows / tc::kConvWarps;  // rows per converter warp
+          constexpr int NL = RPW / 2;                       // float4 loads per lane
+          uint4 v[NL];  // raw fp32 bits
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int rl = cw * 32 + 2 * i + half;
-            v[i] = (rl < nrows) ? *reinterpret_cast<const float4*>(stg + s * tc::kStgBytes + rl * 256 + kq * 4)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i = 0; i < NL; ++i) {
+            const int rl = cw * RPW + 2 * i + half;
+            v[i] = (rl < nrows) ? *reinterpret_cast<const uint4*>(stg + s * tc::kStgBytes + rl * 256 + kq * 4)
+                                : make_uint4(0u, 0u, 0u, 0u);
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&stg_empty[s]);  // the staging slot is free once all 4 warps hold their data
-          bool any_lo = false, nonunit = false;
-          uint2 lo_pk[16];
+          if (lane == 0) mbar_arrive(&stg_empty[s]);  // the staging slot is free once every warp holds its rows
+          // Fast path: a non-negative finite value whose low 16 bits are zero is
+          // exactly its upper half in bf16 (spikes 0/1 always are), so the A
+          // operand is two byte permutes per 4 values.  Anything else (low
+          // bits set, negative incl. -0, Inf/NaN: unsigned bits >= 0x7f800000)
+          // sends the warp down the exact path below.
+          uint32_t bits_or = 0u, bits_max = 0u;
+          bool nonunit = false;
+          unsigned char* ahi = a_hi + sa * tc::kABytes;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int rl = cw * 32 + 2 * i + half;
-            const float x[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-            __nv_bfloat16 h[4], l[4];
-            uint32_t nib = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const bool nz = x[e] > 0.0f;
-              nib |= (nz ? 1u : 0u) << e;
-              nonunit |= nz && (x[e] != 1.0f);
-              split_bf16(nz ? x[e] : 0.0f, h[e], l[e]);
-              any_lo |= (__bfloat16_as_ushort(l[e]) & 0x7fffu) != 0;
+          for (int i = 0; i < NL; ++i) {
+            const int rl = cw * RPW + 2 * i + half;
+            const uint4 b = v[i];
+            bits_or |= b.x | b.y | b.z | b.w;
+            bits_max = max(bits_max, max(max(b.x, b.y), max(b.z, b.w)));
+            *reinterpret_cast<uint2*>(ahi + sw128_offset_bf16((uint32_t)rl, (uint32_t)kq)) =
+                make_uint2(__byte_perm(b.x, b.y, 0x7632), __byte_perm(b.z, b.w, 0x7632));
+            if (check_unit) {
+              nonunit |= (b.x != 0u && b.x != 0x3f800000u) || (b.y != 0u && b.y != 0x3f800000u) ||
+                         (b.z != 0u && b.z != 0x3f800000u) || (b.w != 0u && b.w != 0x3f800000u);
             }
-            const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
-            *reinterpret_cast<uint2*>(a_hi + sa * tc::kABytes + off) =
-                make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
-            lo_pk[i] = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
             if (emit) {
               // 32-column words: lanes 16h..16h+7 hold columns 0-31 of the chunk, 16h+8.. columns 32-63
+              const uint32_t nib = (__uint_as_float(b.x) > 0.0f ? 1u : 0u) | (__uint_as_float(b.y) > 0.0f ? 2u : 0u) |
+                                   (__uint_as_float(b.z) > 0.0f ? 4u : 0u) | (__uint_as_float(b.w) > 0.0f ? 8u : 0u);
               uint32_t w = nib << (4 * (lane & 7));
               w |= __shfl_xor_sync(0xffffffffu, w, 1);
               w |= __shfl_xor_sync(0xffffffffu, w, 2);
@@ -318,18 +330,29 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
               }
             }
           }
-          const bool warp_lo = __any_sync(0xffffffffu, any_lo);
+          const bool warp_lo = __any_sync(0xffffffffu, (bits_or & 0xffffu) != 0u || bits_max >= 0x7f800000u);
           if (warp_lo || ((dirty >> sa) & 1u)) {
+            unsigned char* alo = a_lo + sa * tc::kABytes;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int rl = cw * 32 + 2 * i + half;
+            for (int i = 0; i < NL; ++i) {
+              const int rl = cw * RPW + 2 * i + half;
               const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
-              *reinterpret_cast<uint2*>(a_lo + sa * tc::kABytes + off) = warp_lo ? lo_pk[i] : make_uint2(0u, 0u);
+              uint2 lo_pk = make_uint2(0u, 0u);
+              if (warp_lo) {  // exact path: predicate, round-to-nearest hi, lo remainder
+                const float x[4] = {__uint_as_float(v[i].x), __uint_as_float(v[i].y), __uint_as_float(v[i].z),
+                                    __uint_as_float(v[i].w)};
+                __nv_bfloat16 h[4], l[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split_bf16(x[e] > 0.0f ? x[e] : 0.0f, h[e], l[e]);
+                *reinterpret_cast<uint2*>(ahi + off) = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+                lo_pk = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+              }
+              *reinterpret_cast<uint2*>(alo + off) = lo_pk;
             }
             dirty = warp_lo ? (dirty | (1u << sa)) : (dirty & ~(1u << sa));
           }
-          if (emit && a.nonunit && __any_sync(0xffffffffu, nonunit) && lane == 0) atomicOr(a.nonunit, 1);
-          if (lane == 0) lo_flag[sa * 4 + cw] = warp_lo ? 1 : 0;
+          if (check_unit && __any_sync(0xffffffffu, nonunit) && lane == 0) atomicOr(a.nonunit, 1);
+          if (lane == 0) lo_flag[sa * tc::kConvWarps + cw] = warp_lo ? 1 : 0;
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[sa]);
@@ -338,7 +361,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 6-9)
+    // ---------------------------------------------------------------- epilogue (warps 10-13)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     for (int g = 0; g < groups; ++g) {
       const int tg = min(G, tiles - g * G);
@@ -349,29 +372,34 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         const int64_t row = r_begin + (int64_t)(g * G + t) * tc::kRows + q * 32 + lane;
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
 #pragma unroll 1
-        for (int c = 0; c < NT / 16; ++c) {
-          float acc[16];
-          tmem_ld16(tbase + (uint32_t)(c * 16), acc);
+        for (int c0 = 0; c0 < NT / 16; c0 += 2) {
+          float acc[2][16];
+          tmem_ld16(tbase + (uint32_t)(c0 * 16), acc[0]);
+          if (c0 + 1 < NT / 16) tmem_ld16(tbase + (uint32_t)((c0 + 1) * 16), acc[1]);
           tmem_wait_ld();
-          const int n = n0 + c * 16;
-          if (row < r_end) {
-            float* y = a.Y + row * a.N + n;
-            if (a.y_vec && n + 16 <= a.N) {
 #pragma unroll
-              for (int gq = 0; gq < 4; ++gq) {
-                float4 o = make_float4(acc[4 * gq], acc[4 * gq + 1], acc[4 * gq + 2], acc[4 * gq + 3]);
-                if (a.bias) {
-                  o.x += a.bias[n + 4 * gq];
-                  o.y += a.bias[n + 4 * gq + 1];
-                  o.z += a.bias[n + 4 * gq + 2];
-                  o.w += a.bias[n + 4 * gq + 3];
+          for (int h = 0; h < 2; ++h) {
+            const int c = c0 + h;
+            const int n = n0 + c * 16;
+            if (c < NT / 16 && row < r_end) {
+              float* y = a.Y + row * a.N + n;
+              if (a.y_vec && n + 16 <= a.N) {
+#pragma unroll
+                for (int gq = 0; gq < 4; ++gq) {
+                  float4 o = make_float4(acc[h][4 * gq], acc[h][4 * gq + 1], acc[h][4 * gq + 2], acc[h][4 * gq + 3]);
+                  if (a.bias) {
+                    o.x += a.bias[n + 4 * gq];
+                    o.y += a.bias[n + 4 * gq + 1];
+                    o.z += a.bias[n + 4 * gq + 2];
+                    o.w += a.bias[n + 4 * gq + 3];
+                  }
+                  *reinterpret_cast<float4*>(y + 4 * gq) = o;
                 }
-                *reinterpret_cast<float4*>(y + 4 * gq) = o;
-              }
-            } else {
+              } else {
 #pragma unroll
-              for (int e = 0; e < 16; ++e)
-                if (n + e < a.N) y[e] = a.bias ? acc[e] + a.bias[n + e] : acc[e];
+                for (int e = 0; e < 16; ++e)
+                  if (n + e < a.N) y[e] = a.bias ? acc[h][e] + a.bias[n + e] : acc[h][e];
+              }
             }
           }
         }
