@@ -79,15 +79,27 @@ struct CsrArgs {
   uint64_t* tile_desc;
   uint64_t* plane_desc;
   uint8_t* tile_flags;     // [num_tiles]: 1 if the tile holds a positive value != 1
-  const uint32_t* bitmap;  // bitmap source: [T*M][KW] packed spikes written by the dense kernel
+  const uint32_t* bitmap;  // bitmap source: [T*M][KWP] planar spike masks written by the dense kernel
   const int32_t* row_cnt;  // bitmap source: [T*M] spikes per row
+  int KWP;                 // planar words per row (2 per 64-column chunk)
+  const int32_t* blk_sum;                // bitmap source: spikes per 128-row block of the T*M rows
+  const unsigned long long* sup_sum;     // bitmap source: spikes per 16384-row super-block
 };
+
+// 8 bits -> bits 0, 4, 8, ..., 28
+__device__ __forceinline__ uint32_t spread8_stride4(uint32_t x) {
+  x = (x | (x << 12)) & 0x000f000fu;
+  x = (x | (x << 6)) & 0x03030303u;
+  x = (x | (x << 3)) & 0x11111111u;
+  return x;
+}
 
 __device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
   uint64_t d = ld_relaxed_u64(p);
   if ((d >> 62) != 0) return d;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);  // back off: polling costs issue slots of the working warps
     d = ld_relaxed_u64(p);
     if ((d >> 62) != 0) return d;
     if ((it & 31u) == 0 && global_ns() - t0 > kSpinLimitNs) {
@@ -110,8 +122,13 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
   __shared__ int64_t s_excl, s_base;
   __shared__ unsigned int s_tile;
   __shared__ int s_nonunit;
+  __shared__ int64_t s_pre_tile, s_pre_plane, s_red[8][2];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // after a dense pass this grid is a programmatic dependent: its inputs
+  // (bitmap, counts, cleared scan state) are complete only after this wait
+  // (a no-op for an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     s_tile = atomicAdd(&a.state->tile_counter, 1u);
     s_nonunit = 0;
@@ -128,11 +145,57 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
   // ---- phase A: ballot rows into the shared bitmap
   bool nonunit = false;
   if (FROM_BITMAP) {
+    // Planar masks of the dense kernel: per row and 64-column chunk c two
+    // words P0 = M0 | M1 << 16, P1 = M2 | M3 << 16, bit m of plane Me being
+    // column 64c + 4m + e.  Column-order word 2c (+1) takes bits 0-7 (8-15)
+    // of every plane, spread to every 4th bit and offset by e.
     const int64_t grow0 = (int64_t)plane * a.M + row0;
-    const uint32_t* src = a.bitmap + grow0 * a.KW;
-    for (int64_t i = threadIdx.x; i < (int64_t)rows * a.KW; i += blockDim.x) bm[i] = src[i];
+    const int nch = a.KWP / 2;
+    const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow0 * a.KWP);
+    for (int64_t i = threadIdx.x; i < (int64_t)rows * nch; i += blockDim.x) {
+      const int r = (int)(i / nch), c = (int)(i % nch);
+      const uint2 pw = src[(int64_t)r * nch + c];
+      const uint32_t planes[4] = {pw.x & 0xffffu, pw.x >> 16, pw.y & 0xffffu, pw.y >> 16};
+      uint32_t w0 = 0u, w1 = 0u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        w0 |= spread8_stride4(planes[e] & 0xffu) << e;
+        w1 |= spread8_stride4(planes[e] >> 8) << e;
+      }
+      if (2 * c < a.KW) bm[r * a.KW + 2 * c] = w0;
+      if (2 * c + 1 < a.KW) bm[r * a.KW + 2 * c + 1] = w1;
+    }
     for (int r = threadIdx.x; r < RT; r += blockDim.x) cnt[r] = (r < rows) ? a.row_cnt[grow0 + r] : 0;
     if (threadIdx.x == 0) s_nonunit = a.state->nonunit != 0;
+    // Global prefix of a row from the dense pass's sums: whole 16384-row
+    // super-blocks, then whole 128-row blocks, then single rows -- at most
+    // R/16384 + 127 + 127 reads, spread over the CTA (no look-back, no wait).
+    int64_t part[2] = {0, 0};
+    const int64_t at[2] = {grow0, (int64_t)plane * a.M};
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t r = at[q];
+      const int64_t s_end = r >> 14, b0 = s_end << 7, b1 = r >> 7;
+      for (int64_t i = threadIdx.x; i < s_end; i += blockDim.x) part[q] += (int64_t)a.sup_sum[i];
+      for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) part[q] += a.blk_sum[i];
+      for (int64_t i = (b1 << 7) + threadIdx.x; i < r; i += blockDim.x) part[q] += a.row_cnt[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part[q] += __shfl_xor_sync(0xffffffffu, part[q], o);
+    }
+    if (lane == 0) {
+      s_red[warp][0] = part[0];
+      s_red[warp][1] = part[1];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int64_t t0 = 0, t1 = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        t0 += s_red[w][0];
+        t1 += s_red[w][1];
+      }
+      s_pre_tile = t0;
+      s_pre_plane = t1;
+    }
   }
   for (int r = warp; r < RT && !FROM_BITMAP; r += 8) {
     int c = 0;
@@ -180,7 +243,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
     const int64_t agg = running;
     bool ok = true;
     int64_t excl = 0;
-    if (valid_tile && tile > 0) {
+    if (!FROM_BITMAP && valid_tile && tile > 0) {
       // warp-wide look-back: lane l probes tile j - l, 32 predecessors per
       // round; the nearest inclusive prefix ends the walk.
       if (lane == 0) st_relaxed_u64(&a.tile_desc[tile], kDescAgg | (uint64_t)agg);
@@ -198,17 +261,28 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
       }
       ok = __all_sync(0xffffffffu, ok);
     }
+    if (FROM_BITMAP) {
+      excl = s_pre_tile;  // computed from the dense pass's block sums (below)
+    }
     if (lane == 0 && valid_tile) {
-      st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
       int64_t base;
-      if (tip == 0) {
-        base = excl;
-        st_relaxed_u64(&a.plane_desc[plane], kDescIncl | (uint64_t)base);
-        a.plane_ptr[plane] = base;
-        a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
+      if (FROM_BITMAP) {
+        base = s_pre_plane;
+        if (tip == 0) {
+          a.plane_ptr[plane] = base;
+          a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
+        }
       } else {
-        const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
-        base = (int64_t)(d & kDescValueMask);
+        st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
+        if (tip == 0) {
+          base = excl;
+          st_relaxed_u64(&a.plane_desc[plane], kDescIncl | (uint64_t)base);
+          a.plane_ptr[plane] = base;
+          a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
+        } else {
+          const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
+          base = (int64_t)(d & kDescValueMask);
+        }
       }
       if (plane == a.T - 1 && tip == a.tiles_per_plane - 1) a.plane_ptr[a.T] = excl + agg;
       a.tile_flags[tile] = s_nonunit ? 1 : 0;
@@ -227,24 +301,29 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
       rp[r] = (int32_t)(rel + pre[r] + cnt[r]);
       if (nr) nr[r] = cnt[r];
     }
-    // Expansion: lane l takes word w0 + l of the row, a warp scan of the word
-    // popcounts gives each lane its output offset, and the lane writes its
-    // word's columns in ascending order.
+    // Expansion: a segment of LPR lanes (LPR = words per row rounded up to a
+    // power of two, at most 32) takes one row; lane l of the segment takes
+    // word w0 + l, a segmented scan of the word popcounts gives its output
+    // offset, and the lane writes its word's columns in ascending order.
     bool overflow = false;
     const bool unit_values = FROM_BITMAP && !s_nonunit;  // spikes of value 1 need no gather from S
-    for (int r = warp; r < rows; r += 8) {
-      int64_t pos = excl + pre[r];
-      const uint32_t* bw = bm + r * a.KW;
-      const float* row = Sp + (int64_t)r * a.K;
-      for (int w0 = 0; w0 < a.KW; w0 += 32) {
-        const int w = w0 + lane;
-        uint32_t bits = (w < a.KW) ? bw[w] : 0u;
+    int LPR = 1;
+    while (LPR < a.KW && LPR < 32) LPR <<= 1;
+    const int seg = lane / LPR, sl = lane % LPR, nseg = 32 / LPR;
+    for (int rb = warp * nseg; rb < rows; rb += 8 * nseg) {
+      const int r = rb + seg;
+      const bool active = r < rows;
+      int64_t pos = active ? excl + pre[r] : 0;
+      const uint32_t* bw = bm + (active ? r : 0) * a.KW;
+      const float* row = Sp + (int64_t)(active ? r : 0) * a.K;
+      for (int w0 = 0; w0 < a.KW; w0 += LPR) {
+        const int w = w0 + sl;
+        uint32_t bits = (active && w < a.KW) ? bw[w] : 0u;
         const int c = __popc(bits);
         int incl = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
+        for (int o = 1; o < LPR; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o, LPR);
+          if (sl >= o) incl += y;
         }
         int64_t p = pos + (incl - c);
         while (bits) {
@@ -259,7 +338,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
           }
           ++p;
         }
-        pos += __shfl_sync(0xffffffffu, incl, 31);
+        pos += __shfl_sync(0xffffffffu, incl, LPR - 1, LPR);
       }
     }
     if (__any_sync(0xffffffffu, overflow) && lane == 0) report_device_error(SPK_DEV_CSR_OVERFLOW);
@@ -271,7 +350,8 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 // set, the scan reads the packed spikes and row counts of a preceding dense
 // pass instead of S (S is then only read for values of non-unit spikes), and
 // `state_zeroed` says that pass already cleared the scan state.
-int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* row_cnt, bool state_zeroed, int T,
+int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* row_cnt, const int32_t* blk_sum,
+                       const unsigned long long* sup_sum, bool state_zeroed, int T,
                        int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
                        int64_t* plane_ptr, int64_t col_capacity, void* ws, cudaStream_t stream,
                        const uint8_t** tile_flags_out, CsrLayout* layout_out) {
@@ -298,6 +378,9 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   a.tile_flags = reinterpret_cast<uint8_t*>(base + L.flags_off);
   a.bitmap = bitmap;
   a.row_cnt = row_cnt;
+  a.KWP = 2 * (int)ceil_div(K, 64);
+  a.blk_sum = blk_sum;
+  a.sup_sum = sup_sum;
   const size_t smem = (size_t)L.rows_per_tile * L.KW * 4 + (size_t)L.rows_per_tile * 8;
   auto kern = bitmap ? csr_scan_kernel<true> : csr_scan_kernel<false>;
   if (smem > 48 * 1024) {
@@ -308,7 +391,12 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   // can be shared with any other use between calls.
   if (!state_zeroed) SPK_CUDA_TRY(cudaMemsetAsync(base, 0, L.flags_off, stream));
   prof_before(SPK_KERNEL_CSR_SCAN, stream);
-  kern<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
+  if (bitmap) {
+    // follows the dense kernel on the stream: programmatic dependent launch
+    SPK_CUDA_TRY(launch_dependent(kern, dim3((unsigned)L.num_tiles), dim3(256), smem, stream, a));
+  } else {
+    kern<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
+  }
   prof_after(SPK_KERNEL_CSR_SCAN, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
@@ -320,7 +408,7 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
 int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
                     int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
                     cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out) {
-  return launch_csr_scan_ex(S, nullptr, nullptr, false, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
+  return launch_csr_scan_ex(S, nullptr, nullptr, nullptr, nullptr, false, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
                             col_capacity, ws, stream, tile_flags_out, layout_out);
 }
 

@@ -12,6 +12,9 @@ namespace spk {
 
 struct SlLayout {
   size_t csr_state;     // look-back state of the CSR scan (cleared every call)
+  size_t blk_sum;       // spikes per 128-row block (dense path; cleared every call)
+  size_t sup_sum;       // spikes per 16384-row super-block
+  size_t zero_end;      // [csr_state, zero_end) is cleared by the weight-image kernel
   size_t img;           // W image (dense branch)
   size_t bitmap;        // packed spikes [T*M][ceil(K/32)] written by the dense kernel for the scan
   size_t row_cnt;       // spikes per row [T*M]
@@ -36,10 +39,15 @@ inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool inte
   size_t off = 0;
   L.csr_state = off;
   off += align_up(csr_layout(T, M, K).total, 256);
+  L.blk_sum = off;
+  off += align_up(sizeof(int32_t) * (size_t)ceil_div((int64_t)T * M, 128), 256);
+  L.sup_sum = off;
+  off += align_up(sizeof(uint64_t) * (size_t)ceil_div((int64_t)T * M, 16384), 256);
+  L.zero_end = off;
   L.img = off;
   off += align_up(tc_plan(K, N, w_dtype).img_bytes, 1024);
   L.bitmap = off;
-  off += align_up(sizeof(uint32_t) * (size_t)T * M * ((K + 31) / 32), 256);
+  off += align_up(sizeof(uint32_t) * (size_t)T * M * (2 * ((K + 63) / 64)), 256);  // planar masks
   L.row_cnt = off;
   off += align_up(sizeof(int32_t) * (size_t)T * M, 256);
   if (internal_csr) {
@@ -81,21 +89,23 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
     // bitmap and row counts; the scan expands them (no second read of S).
     const TcPlan p = tc_plan(K, N, w_dtype);
     unsigned char* img = reinterpret_cast<unsigned char*>(wsb + L.img);
-    const CsrLayout cl = csr_layout(T, M, K);
     uint32_t* state = reinterpret_cast<uint32_t*>(wsb + L.csr_state);
     rc = launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr,
-                        want_csr ? (int64_t)(cl.flags_off / 4) : 0, stream);
+                        want_csr ? (int64_t)((L.zero_end - L.csr_state) / 4) : 0, stream);
     if (rc) return rc;
-    TcOut o{bias, Y, nullptr, nullptr, nullptr};
+    TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
     if (want_csr) {
       o.bitmap = reinterpret_cast<uint32_t*>(wsb + L.bitmap);
       o.row_cnt = reinterpret_cast<int32_t*>(wsb + L.row_cnt);
-      o.nonunit = reinterpret_cast<int*>(wsb + L.csr_state) + 1;  // ScanState::nonunit
+      o.blk_sum = reinterpret_cast<int32_t*>(wsb + L.blk_sum);
+      o.sup_sum = reinterpret_cast<unsigned long long*>(wsb + L.sup_sum);
+      // value check only when CSR values are requested (spikes of 1 need no gather)
+      if (values) o.nonunit = reinterpret_cast<int*>(wsb + L.csr_state) + 1;  // ScanState::nonunit
     }
     rc = launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
     if (rc) return rc;
     if (want_csr) {
-      rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
+      rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, o.blk_sum, o.sup_sum, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
                               col_capacity, wsb + L.csr_state, stream, nullptr, nullptr);
     }
     return rc;

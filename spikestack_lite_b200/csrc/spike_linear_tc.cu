@@ -76,15 +76,17 @@ struct Cfg {
 
 struct TcArgs {
   int64_t R;              // rows (T*M)
-  int K, N, nk, KW;       // nk: 64-wide K chunks; KW: 32-bit bitmap words per row
+  int K, N, nk, KWP;      // nk: 64-wide K chunks; KWP = 2*nk: planar bitmap words per row
   const unsigned char* wimg;
   const float* bias;
   float* Y;
   int y_vec;              // Y 16-byte aligned and N % 4 == 0
   int64_t rows_per_cta;   // multiple of 32
-  uint32_t* bitmap;       // [R][KW] packed spikes (bit k%32 of word k/32), or null
+  uint32_t* bitmap;       // [R][KWP] planar spike masks (see the converter), or null
   int32_t* row_cnt;       // [R] spikes per row, or null
   int* nonunit;           // set to 1 when a positive value other than 1 is seen
+  int32_t* blk_sum;       // spikes per 128-row block (for the CSR scan's prefixes)
+  unsigned long long* sup_sum;  // spikes per 16384-row super-block
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -161,6 +163,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched as a programmatic dependent of the weight-image kernel: the
+  // prologue above overlaps its tail; its outputs (image, cleared scan state)
+  // are read only after this wait.  The CSR scan may launch early in turn.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -292,6 +299,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           // sends the warp down the exact path below.
           uint32_t bits_or = 0u, bits_max = 0u;
           bool nonunit = false;
+          uint32_t keep0 = 0u, keep1 = 0u;  // lane L (< 16) ends with the planar spike mask of local row L
           unsigned char* ahi = a_hi + sa * tc::kABytes;
 #pragma unroll
           for (int i = 0; i < NL; ++i) {
@@ -306,28 +314,46 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                          (b.z != 0u && b.z != 0x3f800000u) || (b.w != 0u && b.w != 0x3f800000u);
             }
             if (emit) {
-              // 32-column words: lanes 16h..16h+7 hold columns 0-31 of the chunk, 16h+8.. columns 32-63
-              const uint32_t nib = (__uint_as_float(b.x) > 0.0f ? 1u : 0u) | (__uint_as_float(b.y) > 0.0f ? 2u : 0u) |
-                                   (__uint_as_float(b.z) > 0.0f ? 4u : 0u) | (__uint_as_float(b.w) > 0.0f ? 8u : 0u);
-              uint32_t w = nib << (4 * (lane & 7));
-              w |= __shfl_xor_sync(0xffffffffu, w, 1);
-              w |= __shfl_xor_sync(0xffffffffu, w, 2);
-              w |= __shfl_xor_sync(0xffffffffu, w, 4);
-              const uint32_t w_hi = __shfl_down_sync(0xffffffffu, w, 8);
-              if ((lane & 15) == 0 && rl < nrows) {
-                const int64_t grow = row0 + rl;
-                const int idx = t * tc::kRows + rl;
-                const int c = __popc(w) + (kc * 2 + 1 < a.KW ? __popc(w_hi) : 0);
-                row_count[idx] = (kc == 0 ? 0 : row_count[idx]) + c;
-                uint32_t* bw = a.bitmap + grow * a.KW + kc * 2;
-                if (kc * 2 + 1 < a.KW && ((reinterpret_cast<uintptr_t>(bw) & 7) == 0)) {
-                  *reinterpret_cast<uint2*>(bw) = make_uint2(w, w_hi);
-                } else {
-                  bw[0] = w;
-                  if (kc * 2 + 1 < a.KW) bw[1] = w_hi;
-                }
-                if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = row_count[idx];
+              // Planar spike masks: ballot e has bit m of lanes 0-15 = column 4m+e of
+              // row 2i, of lanes 16-31 = column 4m+e of row 2i+1.  Per row and
+              // 64-column chunk, the 4 16-bit planes are packed into 2 words
+              // (P0 = M0 | M1 << 16, P1 = M2 | M3 << 16); the CSR scan converts
+              // them to column order when it loads them.
+              const uint32_t m0 = __ballot_sync(0xffffffffu, __uint_as_float(b.x) > 0.0f);
+              const uint32_t m1 = __ballot_sync(0xffffffffu, __uint_as_float(b.y) > 0.0f);
+              const uint32_t m2 = __ballot_sync(0xffffffffu, __uint_as_float(b.z) > 0.0f);
+              const uint32_t m3 = __ballot_sync(0xffffffffu, __uint_as_float(b.w) > 0.0f);
+              if (lane == 2 * i) {
+                keep0 = __byte_perm(m0, m1, 0x5410);
+                keep1 = __byte_perm(m2, m3, 0x5410);
+              } else if (lane == 2 * i + 1) {
+                keep0 = __byte_perm(m0, m1, 0x7632);
+                keep1 = __byte_perm(m2, m3, 0x7632);
               }
+            }
+          }
+          if (emit && lane < RPW) {
+            const int rl = cw * RPW + lane;
+            if (rl < nrows) {
+              const int64_t grow = row0 + rl;
+              const int idx = t * tc::kRows + rl;
+              const int c = __popc(keep0) + __popc(keep1);
+              const int total = (kc == 0 ? 0 : row_count[idx]) + c;
+              row_count[idx] = total;
+              *reinterpret_cast<uint2*>(a.bitmap + grow * a.KWP + 2 * kc) = make_uint2(keep0, keep1);
+              if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = total;
+            }
+          }
+          if (emit && kc == nk - 1 && a.blk_sum) {
+            // the warp's 16 rows lie in one 128-row block: one atomic per warp and level
+            const int rl = cw * RPW + lane;
+            int v = (lane < RPW && rl < nrows) ? row_count[t * tc::kRows + rl] : 0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const int64_t g0 = row0 + cw * RPW;
+            if (lane == 0 && cw * RPW < nrows && v) {
+              atomicAdd(&a.blk_sum[g0 >> 7], v);
+              atomicAdd(&a.sup_sum[g0 >> 14], (unsigned long long)v);
             }
           }
           const bool warp_lo = __any_sync(0xffffffffu, (bits_or & 0xffffu) != 0u || bits_max >= 0x7f800000u);
@@ -424,22 +450,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 template <typename WT, bool WSPLIT>
 __global__ void w_image_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk, unsigned char* img,
                                uint32_t* zero, int64_t zero_words) {
-  const int64_t total = (int64_t)((N + NT - 1) / NT) * NT * nk * 8;  // one thread per (n, 8 k)
+  // the dense kernel (launched as a programmatic dependent) may start its
+  // prologue now; it waits for this grid before it reads the image
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t total = (int64_t)((N + NT - 1) / NT) * NT * nk * 32;  // one thread per (n, 2 k)
   const size_t half = (size_t)NT * 128;
   const size_t stage = half * (WSPLIT ? 2 : 1);
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = tid; i < zero_words; i += nthr) zero[i] = 0u;
   for (int64_t i = tid; i < total; i += nthr) {
-    const int k8 = (int)(i % 8);
-    const int64_t rest = i / 8;
+    const int k2 = (int)(i % 32);        // pair of columns within the 64-wide chunk
+    const int64_t rest = i / 32;
+    const int64_t ng = rest / nk;        // global n index (padded)
     const int kc = (int)(rest % nk);
-    const int64_t ng = rest / nk;  // global n index (padded)
     const int t = (int)(ng / NT), nl = (int)(ng % NT);
-    __nv_bfloat16 h[8], l[8];
+    __nv_bfloat16 h[2], l[2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int k = kc * 64 + k8 * 8 + e;
+    for (int e = 0; e < 2; ++e) {
+      const int k = kc * 64 + k2 * 2 + e;
       float x = 0.0f;
       if (k < K && ng < N) x = static_cast<float>(W[(int64_t)k * sk + ng * sn]);
       if (WSPLIT) {
@@ -449,13 +478,9 @@ __global__ void w_image_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N
       }
     }
     unsigned char* blk = img + ((size_t)t * nk + kc) * stage;
-    const uint32_t off = sw128_offset_bf16((uint32_t)nl, (uint32_t)(k8 * 8));
-    *reinterpret_cast<uint4*>(blk + off) =
-        make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]), pack_bf16x2(h[6], h[7]));
-    if (WSPLIT) {
-      *reinterpret_cast<uint4*>(blk + half + off) =
-          make_uint4(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]), pack_bf16x2(l[4], l[5]), pack_bf16x2(l[6], l[7]));
-    }
+    const uint32_t off = sw128_offset_bf16((uint32_t)nl, (uint32_t)(k2 * 2));
+    *reinterpret_cast<uint32_t*>(blk + off) = pack_bf16x2(h[0], h[1]);
+    if (WSPLIT) *reinterpret_cast<uint32_t*>(blk + half + off) = pack_bf16x2(l[0], l[1]);
   }
 }
 
@@ -518,6 +543,8 @@ struct TcOut {
   uint32_t* bitmap;
   int32_t* row_cnt;
   int* nonunit;
+  int32_t* blk_sum;
+  unsigned long long* sup_sum;
 };
 
 template <int NT, bool WSPLIT>
@@ -531,7 +558,7 @@ int launch_tc_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t s
   const int64_t gx = ceil_div(a.R, a.rows_per_cta);
   dim3 grid((unsigned)gx, (unsigned)n_tiles);
   prof_before(SPK_KERNEL_DENSE, stream);
-  kern<<<grid, tc::kThreads, C::kSmemBytes, stream>>>(map, a);
+  SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(tc::kThreads), C::kSmemBytes, stream, map, a));
   prof_after(SPK_KERNEL_DENSE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
@@ -540,9 +567,9 @@ int launch_tc_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t s
 
 int launch_w_image(const void* W, int w_dtype, int64_t sk, int64_t sn, int K, int N, const TcPlan& p,
                    unsigned char* img, uint32_t* zero, int64_t zero_words, cudaStream_t stream) {
-  const int64_t total = (int64_t)p.n_tiles * p.NT * p.nk * 8;
+  const int64_t total = (int64_t)p.n_tiles * p.NT * p.nk * 32;
   const int threads = 256;
-  const int blocks = (int)min64(ceil_div(max64(total, zero_words), threads), 4096);
+  const int blocks = (int)min64(ceil_div(max64(total, zero_words), threads), 8192);
   prof_before(SPK_KERNEL_W_IMAGE, stream);
   if (w_dtype == SPK_BF16) {
     w_image_kernel<__nv_bfloat16, false><<<blocks, threads, 0, stream>>>(
@@ -567,7 +594,7 @@ int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.K = K;
   a.N = N;
   a.nk = p.nk;
-  a.KW = (K + 31) / 32;
+  a.KWP = 2 * p.nk;
   a.wimg = img;
   a.bias = o.bias;
   a.Y = o.Y;
@@ -575,6 +602,8 @@ int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.bitmap = o.bitmap;
   a.row_cnt = o.row_cnt;
   a.nonunit = o.nonunit;
+  a.blk_sum = o.blk_sum;
+  a.sup_sum = o.sup_sum;
   if (p.split) {
     switch (p.NT) {
       case 16: return launch_tc_inst<16, true>(map, a, p.n_tiles, stream);

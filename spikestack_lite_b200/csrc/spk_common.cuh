@@ -14,6 +14,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "../../include/spikestack_b200.h"
 
 namespace spk {
@@ -47,6 +49,25 @@ inline int sm_count() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n;
+}
+
+// Launch `kern` as a programmatic dependent of the previous kernel on `stream`:
+// it may start while that kernel drains and must execute griddepcontrol.wait
+// before reading the previous kernel's results.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                    Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -93,31 +114,33 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in hardware until it completes or `hint_ns` passes, instead of
+// re-issuing the test (which would take issue slots from working warps).
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 500000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
-// Bounded wait on the given phase parity.  Also gives up early when *abort
-// (a shared-memory flag other roles set after their own timeout) is raised.
+// Bounded wait on the given phase parity (each try sleeps up to 0.5 ms).
+// Also gives up early when *abort (a shared-memory flag other roles set after
+// their own timeout) is raised.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (abort != nullptr && *abort) return false;
-      if (global_ns() - t0 > kSpinLimitNs) {
-        report_device_error(code);
-        if (abort != nullptr) *abort = 1;
-        return false;
-      }
+    if (abort != nullptr && *abort) return false;
+    if (global_ns() - t0 > kSpinLimitNs) {
+      report_device_error(code);
+      if (abort != nullptr) *abort = 1;
+      return false;
     }
   }
 }
