@@ -325,18 +325,37 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
           const int y = __shfl_up_sync(0xffffffffu, incl, o, LPR);
           if (sl >= o) incl += y;
         }
-        int64_t p = pos + (incl - c);
-        while (bits) {
-          const int b = __ffs(bits) - 1;
-          bits &= bits - 1u;
-          const int col = w * 32 + b;
-          if (p < a.col_capacity) {
-            a.col_idx[p] = col;
-            if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
+        const int64_t p0 = pos + (incl - c);
+        if (p0 + c <= a.col_capacity) {  // common case: 32-bit offsets, no per-entry checks
+          int32_t* dst = a.col_idx + p0;
+          int k = 0;
+          if (a.values == nullptr) {
+            while (bits) {
+              dst[k++] = w * 32 + __ffs(bits) - 1;
+              bits &= bits - 1u;
+            }
           } else {
-            overflow = true;
+            float* vdst = a.values + p0;
+            while (bits) {
+              const int col = w * 32 + __ffs(bits) - 1;
+              bits &= bits - 1u;
+              dst[k] = col;
+              vdst[k++] = unit_values ? 1.0f : row[col];
+            }
           }
-          ++p;
+        } else {
+          int64_t p = p0;
+          while (bits) {
+            const int col = w * 32 + __ffs(bits) - 1;
+            bits &= bits - 1u;
+            if (p < a.col_capacity) {
+              a.col_idx[p] = col;
+              if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
+            } else {
+              overflow = true;
+            }
+            ++p;
+          }
         }
         pos += __shfl_sync(0xffffffffu, incl, LPR - 1, LPR);
       }

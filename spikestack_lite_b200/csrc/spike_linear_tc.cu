@@ -16,16 +16,16 @@
 // side by side in TMEM.  Two accumulator buffers let the epilogue of group g
 // overlap the MMAs of group g+1.
 //
-// Warp roles (448 threads):
+// Warp roles (704 threads):
 //   warp 0     TMA producer: S tiles via a 2-D tensor map (fp32, 32-row x
 //              64-column boxes, zero fill past the tensor edge) into a 3-slot
 //              staging ring; weight chunks of the pre-split image by 1-D bulk
 //              copy.  No multicast anywhere.
 //   warp 1     TMEM owner and MMA issuer (one thread).
-//   warps 2-9  converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
+//   warps 2-17 converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
 //              128-byte-swizzled K-major A layout; optionally the packed spike
 //              bitmap and per-row counts the CSR pass consumes.
-//   warps 10-13 epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
+//   warps 18-21 epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; each role then
 // leaves its loop, issued copies and MMAs are drained, TMEM is freed.
 #include <cuda.h>
@@ -43,7 +43,7 @@ constexpr int kABytes = kRows * 128;    // one A half (hi or lo) of a stage: 16 
 constexpr int kStgBytes = kRows * 256;  // fp32 staging of one stage: 32 KB
 constexpr int kBoxRows = 32;            // TMA box: 32 rows x 64 fp32 = 8 KB
 constexpr int kBoxBytes = kBoxRows * 256;
-constexpr int kConvWarps = 8;           // converter warps
+constexpr int kConvWarps = 16;          // converter warps (8 rows each per stage)
 constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 constexpr int kNS = 3;                  // staging slots
 constexpr int kNA = 2;                  // A slots (hi + lo each)
@@ -256,8 +256,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     }
   } else if (warp < 2 + tc::kConvWarps) {
     // ---------------------------------------------------------------- converters
-    // Warp cw owns rows [16cw, 16cw+16) of each tile; in load i a lane holds
-    // 4 columns of row 16cw + 2i + (lane >> 4).  Fast path: the upper halves
+    // Warp cw owns rows [8cw, 8cw+8) of each tile; in load i a lane holds
+    // 4 columns of row 8cw + 2i + (lane >> 4).  Fast path: the upper halves
     // of the fp32 bits (exact for non-negative values with zero low halves,
     // e.g. spikes) plus a bit test.  Only a warp holding another value (needs
     // the predicate, rounding or a lo half) takes the exact hi/lo split; the
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             }
           }
           if (emit && kc == nk - 1 && a.blk_sum) {
-            // the warp's 16 rows lie in one 128-row block: one atomic per warp and level
+            // the warp's 8 rows lie in one 128-row block: one atomic per warp and level
             const int rl = cw * RPW + lane;
             int v = (lane < RPW && rl < nrows) ? row_count[t * tc::kRows + rl] : 0;
 #pragma unroll
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 10-13)
+    // ---------------------------------------------------------------- epilogue (warps 18-21)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     for (int g = 0; g < groups; ++g) {
       const int tg = min(G, tiles - g * G);
