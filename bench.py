@@ -516,6 +516,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="eager steps only, no JSON metrics (profiling case)")
     ap.add_argument("--rows", type=int, default=None, help="override M (rows per plane) of spike-linear workloads")
+    ap.add_argument("--batch", type=int, default=None, help="override B of the attention workload")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(WORKLOADS[args.workload])
@@ -524,6 +525,9 @@ def main():
     if args.rows is not None:
         cfg["M"] = args.rows
         cfg["name"] += f" (M overridden to {args.rows})"
+    if args.batch is not None and "B" in cfg:
+        cfg["B"] = args.batch
+        cfg["name"] += f" (B overridden to {args.batch})"
     dist = Dist()
 
     if args.impl == "reference":

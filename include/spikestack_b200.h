@@ -64,6 +64,11 @@ int spk_version(void);
 /* Reads (and with clear != 0 resets) the device error word of the current
  * device.  Synchronizes the device. */
 int spk_device_error(int clear, int* out_bits);
+/* Diagnostic for SPK_DEV_PIPE_TIMEOUT: where the first timed-out pipeline
+ * wait gave up since the last clearing spk_device_error call, as
+ * block << 40 | warp << 32 | shared-memory address of the mbarrier (0 when no
+ * wait timed out).  Synchronizes the device. */
+int spk_timeout_site(uint64_t* out_site);
 /* Number of this library's kernel launches issued so far from this process
  * (all threads, all devices).  Used to report gpu_launches. */
 int64_t spk_launch_count(void);

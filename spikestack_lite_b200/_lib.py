@@ -26,6 +26,7 @@ SIGNATURES = {
     "spk_last_error": (_c.c_char_p, []),
     "spk_version": (_I, []),
     "spk_device_error": (_I, [_I, _c.POINTER(_I)]),
+    "spk_timeout_site": (_I, [_c.POINTER(_c.c_uint64)]),
     "spk_launch_count": (_L, []),
     "spk_profile_begin": (_I, [_I]),
     "spk_profile_end": (_I, [_c.POINTER(_c.c_double), _c.POINTER(_L)]),
@@ -155,3 +156,11 @@ def device_error(clear=True):
     bits = ctypes.c_int(0)
     check(load().spk_device_error(1 if clear else 0, ctypes.byref(bits)), "spk_device_error")
     return bits.value
+
+
+def timeout_site():
+    """(block, warp, mbarrier shared address) of the first timed-out pipeline wait, or None."""
+    site = ctypes.c_uint64(0)
+    check(load().spk_timeout_site(ctypes.byref(site)), "spk_timeout_site")
+    v = site.value
+    return None if v == 0 else (v >> 40, (v >> 32) & 0xff, v & 0xffffffff)

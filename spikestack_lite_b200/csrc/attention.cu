@@ -31,6 +31,8 @@ __global__ void normalize_kernel(const float* __restrict__ numer, const float* _
 }
 
 __global__ void decay_table_kernel(const float* __restrict__ lam, int L, int d, float* __restrict__ tab) {
+  // a programmatic dependent (the tensor-core kv pass) may start its prologue
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t total = (int64_t)L * d;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int c = (int)(i % d);
@@ -160,6 +162,9 @@ inline int grid_for(int64_t total, int threads) {
   return (int)min64(ceil_div(total, threads), 148 * 32);
 }
 
+// Workspace: the decay table [L, d], then either the SIMT path's kv blocks
+// [BT, H, dh, dh + 1] or the tensor-core path's per-(bt, head group) images
+// (72 KB each, see attention_tc.cu) -- sized for the larger of the two.
 struct AttnLayout {
   size_t tab, kv, total;
 };
@@ -167,7 +172,9 @@ inline AttnLayout attn_layout(int64_t BT, int L, int H, int dh) {
   AttnLayout A{};
   A.tab = 0;
   A.kv = align_up(sizeof(float) * (size_t)L * H * dh, 256);
-  A.total = A.kv + align_up(sizeof(float) * (size_t)BT * H * dh * (dh + 1), 256);
+  const size_t simt = sizeof(float) * (size_t)BT * H * dh * (dh + 1);
+  const size_t tc = (H * dh) % 128 == 0 ? (size_t)BT * (size_t)(H * dh / 128) * 73728 : 0;
+  A.total = A.kv + align_up(simt > tc ? simt : tc, 256);
   return A;
 }
 
@@ -193,51 +200,5 @@ extern "C" int spk_normalize_attention(const float* numer, const float* denom, i
   spk::normalize_kernel<<<spk::grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(numer, denom, total, eps, out);
   SPK_LAUNCH_CHECK();
   spk::count_launch(1);
-  return SPK_OK;
-}
-
-extern "C" size_t spk_attention_workspace_bytes(int64_t BT, int L, int H, int dh) {
-  if (BT < 1 || L < 1 || H < 1 || dh < 1) return 0;
-  return spk::attn_layout(BT, L, H, dh).total;
-}
-
-extern "C" int spk_spiking_attention(const float* q, const float* k, const float* v, const float* lam, int64_t BT,
-                                     int L, int H, int dh, float eps, float* out, void* workspace,
-                                     size_t workspace_bytes, spk_stream_t stream) {
-  SPK_REQUIRE(q && k && v && lam && out, "q, k, v, lam and out must be non-null");
-  SPK_REQUIRE(BT >= 1 && L >= 1 && H >= 1, "invalid shape");
-  SPK_REQUIRE(dh == 16 || dh == 32 || dh == 64, "head width %d not supported (16, 32 or 64)", dh);
-  SPK_REQUIRE(BT <= 65535, "BT=%lld exceeds the grid limit of 65535", (long long)BT);
-  const spk::AttnLayout A = spk::attn_layout(BT, L, H, dh);
-  if (workspace == nullptr || workspace_bytes < A.total)
-    return spk::fail(SPK_EWORKSPACE, "workspace of %zu bytes required", A.total);
-  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-                               reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
-  SPK_REQUIRE((align_bits & 15) == 0, "q, k, v and out must be 16-byte aligned");
-  cudaStream_t st = (cudaStream_t)stream;
-  float* tab = reinterpret_cast<float*>(static_cast<char*>(workspace) + A.tab);
-  float* kv = reinterpret_cast<float*>(static_cast<char*>(workspace) + A.kv);
-  const int d = H * dh;
-  spk::decay_table_kernel<<<spk::grid_for((int64_t)L * d, 256), 256, 0, st>>>(lam, L, d, tab);
-  SPK_LAUNCH_CHECK();
-  dim3 g1((unsigned)H, (unsigned)BT);
-  dim3 g2((unsigned)spk::ceil_div(L, 64), (unsigned)H, (unsigned)BT);
-  spk::prof_before(SPK_KERNEL_ATTN_KV, st);
-  switch (dh) {
-    case 16: spk::attn_kv_kernel<16><<<g1, 32, 0, st>>>(k, v, tab, L, H, kv); break;
-    case 32: spk::attn_kv_kernel<32><<<g1, 64, 0, st>>>(k, v, tab, L, H, kv); break;
-    default: spk::attn_kv_kernel<64><<<g1, 256, 0, st>>>(k, v, tab, L, H, kv); break;
-  }
-  spk::prof_after(SPK_KERNEL_ATTN_KV, st);
-  SPK_LAUNCH_CHECK();
-  spk::prof_before(SPK_KERNEL_ATTN_OUT, st);
-  switch (dh) {
-    case 16: spk::attn_out_kernel<16><<<g2, 256, 0, st>>>(q, kv, L, H, eps, out); break;
-    case 32: spk::attn_out_kernel<32><<<g2, 256, 0, st>>>(q, kv, L, H, eps, out); break;
-    default: spk::attn_out_kernel<64><<<g2, 256, 0, st>>>(q, kv, L, H, eps, out); break;
-  }
-  spk::prof_after(SPK_KERNEL_ATTN_OUT, st);
-  SPK_LAUNCH_CHECK();
-  spk::count_launch(3);
   return SPK_OK;
 }

@@ -6,5 +6,6 @@
 #include "spike_linear_tc.cu"
 #include "spike_linear.cu"
 #include "attention.cu"
+#include "attention_tc.cu"
 #include "gsmc.cu"
 #include "csr_noalloc.cu"

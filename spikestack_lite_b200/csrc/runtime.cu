@@ -96,8 +96,18 @@ extern "C" int spk_device_error(int clear, int* out_bits) {
   SPK_CUDA_TRY(cudaMemcpyFromSymbol(&bits, spk::g_device_error, sizeof(int)));
   if (clear) {
     const int zero = 0;
+    const unsigned long long none = 0ull;
     SPK_CUDA_TRY(cudaMemcpyToSymbol(spk::g_device_error, &zero, sizeof(int)));
+    SPK_CUDA_TRY(cudaMemcpyToSymbol(spk::g_timeout_site, &none, sizeof(none)));
   }
   if (out_bits != nullptr) *out_bits = bits;
+  return SPK_OK;
+}
+
+extern "C" int spk_timeout_site(uint64_t* out_site) {
+  unsigned long long site = 0ull;
+  SPK_CUDA_TRY(cudaDeviceSynchronize());
+  SPK_CUDA_TRY(cudaMemcpyFromSymbol(&site, spk::g_timeout_site, sizeof(site)));
+  if (out_site != nullptr) *out_site = site;
   return SPK_OK;
 }

@@ -28,10 +28,7 @@
 //   warps 18-21 epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; each role then
 // leaves its loop, issued copies and MMAs are drained, TMEM is freed.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include "spk_common.cuh"
+#include "tma.cuh"
 
 namespace spk {
 
@@ -88,14 +85,6 @@ struct TcArgs {
   int32_t* blk_sum;       // spikes per 128-row block (for the CSR scan's prefixes)
   unsigned long long* sup_sum;  // spikes per 16384-row super-block
 };
-
-__device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst_smem)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
 
 template <int NT, bool WSPLIT>
 __global__ void __launch_bounds__(tc::kThreads, 1)
@@ -172,7 +161,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_s)) : "memory");
+      tma_prefetch_map(&tmap_s);
       int j = 0, jb = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
@@ -290,8 +279,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             v[i] = (rl < nrows) ? *reinterpret_cast<const uint4*>(stg + s * tc::kStgBytes + rl * 256 + kq * 4)
                                 : make_uint4(0u, 0u, 0u, 0u);
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&stg_empty[s]);  // the staging slot is free once every warp holds its rows
           // Fast path: a non-negative finite value whose low 16 bits are zero is
           // exactly its upper half in bf16 (spikes 0/1 always are), so the A
           // operand is two byte permutes per 4 values.  Anything else (low
@@ -332,6 +319,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
               }
             }
           }
+          // The staging slot is released only now: every lane has stored values
+          // computed from its loads, so those loads have completed (a release
+          // right after issuing them could let the next TMA copy overwrite data
+          // that a lane had not read yet).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&stg_empty[s]);
           if (emit && lane < RPW) {
             const int rl = cw * RPW + lane;
             if (rl < nrows) {
@@ -403,6 +396,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           tmem_ld16(tbase + (uint32_t)(c0 * 16), acc[0]);
           if (c0 + 1 < NT / 16) tmem_ld16(tbase + (uint32_t)((c0 + 1) * 16), acc[1]);
           tmem_wait_ld();
+          tmem_reg_fence(acc[0]);
+          if (c0 + 1 < NT / 16) tmem_reg_fence(acc[1]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int c = c0 + h;
@@ -508,33 +503,10 @@ inline bool tc_supported(int K, int N, const void* S) {
   return K >= 1 && N >= 1 && (K % 4) == 0 && (reinterpret_cast<uintptr_t>(S) % 16) == 0;
 }
 
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // S [R, K] fp32 as a 2-D tensor: boxes of 64 columns x 32 rows, zero fill
 // outside the tensor (partial row tiles and K not a multiple of 64).
 static int make_s_map(CUtensorMap* map, const float* S, int64_t R, int K) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return fail(SPK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)R};
-  const cuuint64_t strides[1] = {(cuuint64_t)K * sizeof(float)};
-  const cuuint32_t box[2] = {(cuuint32_t)tc::kKChunk, (cuuint32_t)tc::kBoxRows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(S), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(SPK_ECUDA, "cuTensorMapEncodeTiled failed (%d) for S [%lld, %d]", (int)r,
-                                     (long long)R, K);
-  return SPK_OK;
+  return make_map_2d_f32(map, S, R, K, K, tc::kKChunk, tc::kBoxRows, "S");
 }
 
 struct TcOut {

@@ -78,6 +78,9 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Device error word (per device; read and cleared by spk_device_error()).
 // Defined here: the library is built as one translation unit (engine.cu).
 __device__ int g_device_error = 0;
+// Where the first timed-out pipeline wait gave up: block << 40 | warp << 32 |
+// shared-memory address of the mbarrier (0 = none).
+__device__ unsigned long long g_timeout_site = 0ull;
 
 // ----------------------------------------------------------- device helpers
 #ifdef __CUDACC__
@@ -139,6 +142,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (abort != nullptr && *abort) return false;
     if (global_ns() - t0 > kSpinLimitNs) {
       report_device_error(code);
+      atomicCAS(&g_timeout_site, 0ull,
+                ((unsigned long long)blockIdx.x << 40) | ((unsigned long long)(threadIdx.x >> 5) << 32) | smem_u32(bar));
       if (abort != nullptr) *abort = 1;
       return false;
     }
@@ -192,6 +197,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.ld fills its destination registers asynchronously; the compiler sees
+// them as written by the ld statement and may schedule their uses before
+// tcgen05.wait::ld.  Passing them through an empty volatile statement placed
+// after the wait makes every use depend on it.
+__device__ __forceinline__ void tmem_reg_fence(float (&v)[16]) {
+  asm volatile(""
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                 "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
+                 "+f"(v[15]));
+}
 
 // 32 data-path lanes x 32 bit, 16 consecutive columns: thread i of the warp
 // receives columns [col, col+16) of TMEM lane (lane_base + i).
@@ -223,16 +238,37 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_kmajor(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N) {
+// Shared-memory descriptor of an MN-major bf16 operand with 128-byte swizzle:
+// swizzle atoms of 8 K-lines x 64 MN-elements (1024 B, each line 128 B of
+// consecutive MN elements); `mn_stride` = bytes between atoms along MN
+// (leading byte offset), `k_stride` = bytes between atoms along K (stride
+// byte offset).  Atoms start on 1024-byte boundaries.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr, uint32_t mn_stride,
+                                                            uint32_t k_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((k_stride >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32; A and B K-major
+// unless a_mn / b_mn select the MN-major (transposed) operand layout.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N, bool a_mn = false, bool b_mn = false) {
   return (1u << 4)                                // D format f32
          | (1u << 7)                              // A format bf16
          | (1u << 10)                             // B format bf16
+         | (a_mn ? (1u << 15) : 0u)               // A major: MN
+         | (b_mn ? (1u << 16) : 0u)               // B major: MN
          | (static_cast<uint32_t>(N >> 3) << 17)  // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24); // M / 16
 }
 
 // Byte offset of element (r, k) (k in [0, 64)) of a bf16 K-major SW128 block.
+// The swizzle is a function of the address alone, so the same offset serves an
+// MN-major atom with r = the K-line (0-7) and k = the MN element (0-63).
 __host__ __device__ __forceinline__ uint32_t sw128_offset_bf16(uint32_t r, uint32_t k) {
   return r * 128u + ((((k >> 3) ^ (r & 7u)) & 7u) << 4) + ((k & 7u) << 1);
 }

@@ -63,3 +63,51 @@ def test_attention_zero_keys_give_zero_output():
     v = _spk((1, 2, 64, 64), 0.5, 8)
     out = ops.spiking_attention(q, k, v, _lam(64, 9), 2)
     assert torch.count_nonzero(out).item() == 0
+
+
+@pytest.mark.parametrize("shape,heads", [
+    ((4, 64, 64, 512), 8),     # 1024 (bt, head group) units: several per CTA, both accumulator buffers
+    ((2, 3, 100, 128), 2),     # ragged sequence (not a multiple of 32 or 128), dh = 64
+    ((1, 2, 37, 256), 16),     # dh = 16: eight heads per 128-channel group, 37 positions
+    ((1, 1, 300, 384), 12),    # dh = 32, three groups, partial last tile
+])
+def test_tensor_core_attention_geometries(shape, heads):
+    q, k, v = (_spk(shape, 0.15, s) for s in (11, 12, 13))
+    lam = _lam(shape[-1], 14)
+    out = ops.spiking_attention(q, k, v, lam, heads)
+    ref = O.spiking_attention(q.cpu(), k.cpu(), v.cpu(), lam.cpu(), heads)
+    assert O.rel_err(out.cpu().numpy(), ref.numpy()) < TOL
+
+
+def test_tensor_core_attention_real_valued_inputs():
+    """q and v that bf16 does not hold exactly take the hi/lo split passes (k is always split).
+    k stays positive so that the key mass, and so the denominator, is well conditioned."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    shape = (2, 2, 200, 256)
+    q = torch.rand(*shape, generator=g, device="cuda")
+    k = torch.rand(*shape, generator=g, device="cuda")
+    v = torch.randn(*shape, generator=g, device="cuda")
+    lam = _lam(256, 22)
+    out = ops.spiking_attention(q, k, v, lam, 4)
+    ref = O.spiking_attention(q.cpu(), k.cpu(), v.cpu(), lam.cpu(), 4)
+    assert O.rel_err(out.cpu().numpy(), ref.numpy()) < TOL
+
+
+def test_tensor_core_attention_mixed_exactness():
+    """Only some positions hold non-bf16 values: per-warp exact paths next to fast ones."""
+    shape = (1, 4, 256, 128)
+    q, k, v = (_spk(shape, 0.2, s) for s in (31, 32, 33))
+    q[0, 1, 37, 5] = 0.3
+    v[0, 2, 200, 100] = 0.7
+    lam = _lam(128, 34)
+    out = ops.spiking_attention(q, k, v, lam, 2)
+    ref = O.spiking_attention(q.cpu(), k.cpu(), v.cpu(), lam.cpu(), 2)
+    assert O.rel_err(out.cpu().numpy(), ref.numpy()) < TOL
+
+
+def test_tensor_core_attention_zero_keys():
+    q = _spk((1, 3, 130, 128), 0.5, 41)
+    k = torch.zeros_like(q)
+    v = _spk((1, 3, 130, 128), 0.5, 42)
+    out = ops.spiking_attention(q, k, v, _lam(128, 43), 2)
+    assert torch.count_nonzero(out).item() == 0
