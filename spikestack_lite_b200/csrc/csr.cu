@@ -20,6 +20,11 @@
 // Tiles never straddle planes; the first tile of plane t publishes the plane
 // base so that row_ptr is relative to the plane (as in the reference) while
 // col_idx holds the planes back to back.
+//
+// After the dense spike-linear kernel, which already packed the spike masks
+// and counted the spikes per row, 128-row block and 16384-row super-block,
+// csr_from_masks_kernel builds the same CSR without touching S: every prefix
+// is a sum of finished counts (no look-back) and each lane expands one row.
 #include "spk_common.cuh"
 
 namespace spk {
@@ -110,9 +115,6 @@ __device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
   }
 }
 
-// FROM_BITMAP: phase A copies the packed bitmap and the row counts the dense
-// kernel already produced (K/8 bytes per row instead of 4K bytes of S).
-template <bool FROM_BITMAP>
 __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
   extern __shared__ __align__(16) uint32_t smem_u32buf[];
   const int RT = a.rows_per_tile;
@@ -122,13 +124,8 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
   __shared__ int64_t s_excl, s_base;
   __shared__ unsigned int s_tile;
   __shared__ int s_nonunit;
-  __shared__ int64_t s_pre_tile, s_pre_plane, s_red[8][2];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // after a dense pass this grid is a programmatic dependent: its inputs
-  // (bitmap, counts, cleared scan state) are complete only after this wait
-  // (a no-op for an ordinary launch)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     s_tile = atomicAdd(&a.state->tile_counter, 1u);
     s_nonunit = 0;
@@ -144,60 +141,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 
   // ---- phase A: ballot rows into the shared bitmap
   bool nonunit = false;
-  if (FROM_BITMAP) {
-    // Planar masks of the dense kernel: per row and 64-column chunk c two
-    // words P0 = M0 | M1 << 16, P1 = M2 | M3 << 16, bit m of plane Me being
-    // column 64c + 4m + e.  Column-order word 2c (+1) takes bits 0-7 (8-15)
-    // of every plane, spread to every 4th bit and offset by e.
-    const int64_t grow0 = (int64_t)plane * a.M + row0;
-    const int nch = a.KWP / 2;
-    const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow0 * a.KWP);
-    for (int64_t i = threadIdx.x; i < (int64_t)rows * nch; i += blockDim.x) {
-      const int r = (int)(i / nch), c = (int)(i % nch);
-      const uint2 pw = src[(int64_t)r * nch + c];
-      const uint32_t planes[4] = {pw.x & 0xffffu, pw.x >> 16, pw.y & 0xffffu, pw.y >> 16};
-      uint32_t w0 = 0u, w1 = 0u;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        w0 |= spread8_stride4(planes[e] & 0xffu) << e;
-        w1 |= spread8_stride4(planes[e] >> 8) << e;
-      }
-      if (2 * c < a.KW) bm[r * a.KW + 2 * c] = w0;
-      if (2 * c + 1 < a.KW) bm[r * a.KW + 2 * c + 1] = w1;
-    }
-    for (int r = threadIdx.x; r < RT; r += blockDim.x) cnt[r] = (r < rows) ? a.row_cnt[grow0 + r] : 0;
-    if (threadIdx.x == 0) s_nonunit = a.state->nonunit != 0;
-    // Global prefix of a row from the dense pass's sums: whole 16384-row
-    // super-blocks, then whole 128-row blocks, then single rows -- at most
-    // R/16384 + 127 + 127 reads, spread over the CTA (no look-back, no wait).
-    int64_t part[2] = {0, 0};
-    const int64_t at[2] = {grow0, (int64_t)plane * a.M};
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int64_t r = at[q];
-      const int64_t s_end = r >> 14, b0 = s_end << 7, b1 = r >> 7;
-      for (int64_t i = threadIdx.x; i < s_end; i += blockDim.x) part[q] += (int64_t)a.sup_sum[i];
-      for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) part[q] += a.blk_sum[i];
-      for (int64_t i = (b1 << 7) + threadIdx.x; i < r; i += blockDim.x) part[q] += a.row_cnt[i];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part[q] += __shfl_xor_sync(0xffffffffu, part[q], o);
-    }
-    if (lane == 0) {
-      s_red[warp][0] = part[0];
-      s_red[warp][1] = part[1];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int64_t t0 = 0, t1 = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-        t0 += s_red[w][0];
-        t1 += s_red[w][1];
-      }
-      s_pre_tile = t0;
-      s_pre_plane = t1;
-    }
-  }
-  for (int r = warp; r < RT && !FROM_BITMAP; r += 8) {
+  for (int r = warp; r < RT; r += 8) {
     int c = 0;
     if (r < rows) {
       const float* row = Sp + (int64_t)r * a.K;
@@ -243,7 +187,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
     const int64_t agg = running;
     bool ok = true;
     int64_t excl = 0;
-    if (!FROM_BITMAP && valid_tile && tile > 0) {
+    if (valid_tile && tile > 0) {
       // warp-wide look-back: lane l probes tile j - l, 32 predecessors per
       // round; the nearest inclusive prefix ends the walk.
       if (lane == 0) st_relaxed_u64(&a.tile_desc[tile], kDescAgg | (uint64_t)agg);
@@ -261,28 +205,17 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
       }
       ok = __all_sync(0xffffffffu, ok);
     }
-    if (FROM_BITMAP) {
-      excl = s_pre_tile;  // computed from the dense pass's block sums (below)
-    }
     if (lane == 0 && valid_tile) {
       int64_t base;
-      if (FROM_BITMAP) {
-        base = s_pre_plane;
-        if (tip == 0) {
-          a.plane_ptr[plane] = base;
-          a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
-        }
+      st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
+      if (tip == 0) {
+        base = excl;
+        st_relaxed_u64(&a.plane_desc[plane], kDescIncl | (uint64_t)base);
+        a.plane_ptr[plane] = base;
+        a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
       } else {
-        st_relaxed_u64(&a.tile_desc[tile], kDescIncl | (uint64_t)(excl + agg));
-        if (tip == 0) {
-          base = excl;
-          st_relaxed_u64(&a.plane_desc[plane], kDescIncl | (uint64_t)base);
-          a.plane_ptr[plane] = base;
-          a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
-        } else {
-          const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
-          base = (int64_t)(d & kDescValueMask);
-        }
+        const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
+        base = (int64_t)(d & kDescValueMask);
       }
       if (plane == a.T - 1 && tip == a.tiles_per_plane - 1) a.plane_ptr[a.T] = excl + agg;
       a.tile_flags[tile] = s_nonunit ? 1 : 0;
@@ -306,7 +239,6 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
     // word w0 + l, a segmented scan of the word popcounts gives its output
     // offset, and the lane writes its word's columns in ascending order.
     bool overflow = false;
-    const bool unit_values = FROM_BITMAP && !s_nonunit;  // spikes of value 1 need no gather from S
     int LPR = 1;
     while (LPR < a.KW && LPR < 32) LPR <<= 1;
     const int seg = lane / LPR, sl = lane % LPR, nseg = 32 / LPR;
@@ -340,7 +272,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
               const int col = w * 32 + __ffs(bits) - 1;
               bits &= bits - 1u;
               dst[k] = col;
-              vdst[k++] = unit_values ? 1.0f : row[col];
+              vdst[k++] = row[col];
             }
           }
         } else {
@@ -350,7 +282,7 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
             bits &= bits - 1u;
             if (p < a.col_capacity) {
               a.col_idx[p] = col;
-              if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
+              if (a.values) a.values[p] = row[col];
             } else {
               overflow = true;
             }
@@ -369,6 +301,178 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 // set, the scan reads the packed spikes and row counts of a preceding dense
 // pass instead of S (S is then only read for values of non-unit spikes), and
 // `state_zeroed` says that pass already cleared the scan state.
+// Spikes before global rows r0 and r1 of the T*M rows, from the dense
+// kernel's sums: whole 16384-row super-blocks, whole 128-row blocks, then
+// single rows (at most R/16384 + 127 + 127 reads each), reduced over the CTA
+// in one pass.  Call from every thread; `red` is [2][warps] shared scratch.
+__device__ __forceinline__ void prefix_from_sums(const CsrArgs& a, int64_t r0, int64_t r1, int64_t* red,
+                                                 int64_t& p0, int64_t& p1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (int)(blockDim.x >> 5);
+  int64_t part[2] = {0, 0};
+  const int64_t at[2] = {r0, r1};
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int64_t r = at[q];
+    const int64_t s_end = r >> 14, b0 = s_end << 7, b1 = r >> 7;
+    for (int64_t i = threadIdx.x; i < s_end; i += blockDim.x) part[q] += (int64_t)a.sup_sum[i];
+    for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) part[q] += a.blk_sum[i];
+    for (int64_t i = (b1 << 7) + threadIdx.x; i < r; i += blockDim.x) part[q] += a.row_cnt[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+    part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
+  }
+  if (lane == 0) {
+    red[warp] = part[0];
+    red[nw + warp] = part[1];
+  }
+  __syncthreads();
+  p0 = 0;
+  p1 = 0;
+  for (int w = 0; w < nw; ++w) {
+    p0 += red[w];
+    p1 += red[nw + w];
+  }
+}
+
+// CSR from the dense kernel's planar spike masks (row counts and block sums
+// come with them): one row per lane, 128 rows per CTA.  For every 64-column
+// chunk a lane rebuilds the two column-order words from the four 16-bit
+// planes with a shared 8-bit spread table and writes the set columns in
+// ascending order to its row's segment.  No look-back and no waiting: every
+// prefix is a sum of counts that are complete when the grid starts.
+// Column indices of a warp's 32 rows are contiguous in col_idx: lanes expand
+// into a per-warp shared buffer and the warp copies it out with coalesced
+// stores (a warp whose rows hold more than kWarpBuf spikes, or whose values
+// are requested, writes straight to global memory).
+constexpr int kMaskRows = 128;
+constexpr int kMaskWarps = kMaskRows / 32;
+constexpr int kWarpBuf = 2048;
+constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
+
+__global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
+  extern __shared__ __align__(16) int32_t s_buf_all[];  // [kMaskWarps][kWarpBuf]
+  __shared__ uint32_t s_spread[256];
+  __shared__ int64_t s_red[2 * kMaskWarps];
+  __shared__ int s_wtot[kMaskWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 256; i += kMaskRows) s_spread[i] = spread8_stride4(i);
+  // programmatic dependent of the dense kernel: its outputs are complete after this
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int plane = (int)(blockIdx.x / tiles_pp);
+  const int64_t row0 = (blockIdx.x % tiles_pp) * kMaskRows;  // row within the plane
+  const int64_t grow0 = (int64_t)plane * a.M + row0;
+  const int64_t r = row0 + threadIdx.x;
+  const bool valid = r < a.M;
+  const int64_t grow = grow0 + threadIdx.x;
+  const int cnt = valid ? a.row_cnt[grow] : 0;
+  const int nch = a.KWP / 2;
+  const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow * a.KWP);
+  constexpr int kPre = 8;  // mask chunks fetched ahead of the prefix computation
+  uint2 pre_w[kPre];
+#pragma unroll
+  for (int c = 0; c < kPre; ++c) pre_w[c] = (cnt > 0 && c < nch) ? __ldg(src + c) : make_uint2(0u, 0u);
+  int64_t pre_tile, pre_plane;
+  prefix_from_sums(a, grow0, (int64_t)plane * a.M, s_red, pre_tile, pre_plane);
+  // exclusive prefix of the row counts inside the CTA
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_wtot[warp] = incl;
+  __syncthreads();
+  int wbase = 0, ctot = 0;
+#pragma unroll
+  for (int w = 0; w < kMaskWarps; ++w) {
+    wbase += (w < warp) ? s_wtot[w] : 0;
+    ctot += s_wtot[w];
+  }
+  const int64_t pos = pre_tile + wbase + incl - cnt;  // first slot of this row in col_idx
+  const int64_t rel = pre_tile - pre_plane;
+  if (valid) {
+    a.row_ptr[(int64_t)plane * (a.M + 1) + r + 1] = (int32_t)(rel + wbase + incl);
+    if (a.nnz_row) a.nnz_row[grow] = cnt;
+  }
+  if (threadIdx.x == 0) {
+    if (row0 == 0) {
+      a.row_ptr[(int64_t)plane * (a.M + 1)] = 0;
+      a.plane_ptr[plane] = pre_plane;
+    }
+    if (plane == a.T - 1 && row0 + kMaskRows >= a.M) a.plane_ptr[a.T] = pre_tile + ctot;
+  }
+  const int wtot = s_wtot[warp];
+  const int64_t wstart = pre_tile + wbase;
+  const bool staged = a.values == nullptr && wtot <= kWarpBuf && wstart + wtot <= a.col_capacity;
+  int32_t* wbuf = s_buf_all + warp * kWarpBuf;
+  if (cnt > 0) {
+    const bool unit_values = a.state->nonunit == 0;
+    const float* row = a.S + grow * a.K;
+    const bool fits = staged || pos + cnt <= a.col_capacity;
+    int32_t* dst = staged ? wbuf + (incl - cnt) : a.col_idx + (fits ? pos : 0);
+    float* vdst = a.values ? a.values + (fits ? pos : 0) : nullptr;
+    int k = 0;
+    bool overflow = false;
+    for (int c = 0; c < nch; ++c) {
+      uint2 pw;
+      if (c < kPre) {
+#pragma unroll
+        for (int e = 0; e < kPre; ++e)
+          if (e == c) pw = pre_w[e];
+      } else {
+        pw = __ldg(src + c);
+      }
+      if ((pw.x | pw.y) == 0u) continue;
+      // column 64c + 4m + e is bit m of plane e (planes: pw.x lo/hi, pw.y lo/hi)
+      const uint32_t words[2] = {
+          s_spread[pw.x & 0xffu] | (s_spread[(pw.x >> 16) & 0xffu] << 1) | (s_spread[pw.y & 0xffu] << 2) |
+              (s_spread[(pw.y >> 16) & 0xffu] << 3),
+          s_spread[(pw.x >> 8) & 0xffu] | (s_spread[pw.x >> 24] << 1) | (s_spread[(pw.y >> 8) & 0xffu] << 2) |
+              (s_spread[pw.y >> 24] << 3)};
+  #pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t bits = words[h];
+        const int base = 64 * c + 32 * h;
+        if (fits) {
+          if (vdst == nullptr) {
+            while (bits) {
+              dst[k++] = base + __ffs(bits) - 1;
+              bits &= bits - 1u;
+            }
+          } else {
+            while (bits) {
+              const int col = base + __ffs(bits) - 1;
+              bits &= bits - 1u;
+              dst[k] = col;
+              vdst[k++] = unit_values ? 1.0f : row[col];
+            }
+          }
+        } else {
+          while (bits) {
+            const int col = base + __ffs(bits) - 1;
+            bits &= bits - 1u;
+            const int64_t p = pos + k++;
+            if (p < a.col_capacity) {
+              a.col_idx[p] = col;
+              if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
+            } else {
+              overflow = true;
+            }
+          }
+        }
+      }
+    }
+    if (overflow) report_device_error(SPK_DEV_CSR_OVERFLOW);
+  }
+  if (staged) {
+    __syncwarp();
+    int32_t* g = a.col_idx + wstart;
+    for (int i = lane; i < wtot; i += 32) g[i] = wbuf[i];
+  }
+}
+
 int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* row_cnt, const int32_t* blk_sum,
                        const unsigned long long* sup_sum, bool state_zeroed, int T,
                        int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
@@ -400,8 +504,23 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   a.KWP = 2 * (int)ceil_div(K, 64);
   a.blk_sum = blk_sum;
   a.sup_sum = sup_sum;
+  if (bitmap) {
+    // follows the dense kernel on the stream: programmatic dependent launch
+    const int64_t tpp = ceil_div(M, kMaskRows);
+    prof_before(SPK_KERNEL_CSR_SCAN, stream);
+    SPK_CUDA_TRY(cudaFuncSetAttribute(csr_from_masks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kMaskSmem));
+    SPK_CUDA_TRY(launch_dependent(csr_from_masks_kernel, dim3((unsigned)(tpp * T)), dim3(kMaskRows), kMaskSmem,
+                                  stream, a, tpp));
+    prof_after(SPK_KERNEL_CSR_SCAN, stream);
+    SPK_LAUNCH_CHECK();
+    count_launch(1);
+    if (tile_flags_out) *tile_flags_out = nullptr;
+    if (layout_out) *layout_out = L;
+    return SPK_OK;
+  }
   const size_t smem = (size_t)L.rows_per_tile * L.KW * 4 + (size_t)L.rows_per_tile * 8;
-  auto kern = bitmap ? csr_scan_kernel<true> : csr_scan_kernel<false>;
+  auto kern = csr_scan_kernel;
   if (smem > 48 * 1024) {
     SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
@@ -410,12 +529,7 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   // can be shared with any other use between calls.
   if (!state_zeroed) SPK_CUDA_TRY(cudaMemsetAsync(base, 0, L.flags_off, stream));
   prof_before(SPK_KERNEL_CSR_SCAN, stream);
-  if (bitmap) {
-    // follows the dense kernel on the stream: programmatic dependent launch
-    SPK_CUDA_TRY(launch_dependent(kern, dim3((unsigned)L.num_tiles), dim3(256), smem, stream, a));
-  } else {
-    kern<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
-  }
+  kern<<<(unsigned)L.num_tiles, 256, smem, stream>>>(a);
   prof_after(SPK_KERNEL_CSR_SCAN, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);

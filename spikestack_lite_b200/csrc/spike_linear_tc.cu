@@ -258,65 +258,70 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     const int kq = (lane & 15) * 4;
     const bool emit = (a.bitmap != nullptr) && n_tile == 0;
     const bool check_unit = emit && a.nonunit != nullptr;
+    constexpr int RPW = tc::kRows / tc::kConvWarps;  // rows per converter warp
+    constexpr int NL = RPW / 2;                       // 16-byte loads per lane and slot
+    // per-thread offsets, the same for every slot: staging row / A (swizzled) row
+    uint32_t soff[NL], aoff[NL];
+    int rls[NL];
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      rls[i] = cw * RPW + 2 * i + half;
+      soff[i] = (uint32_t)(rls[i] * 256 + kq * 4);
+      aoff[i] = sw128_offset_bf16((uint32_t)rls[i], (uint32_t)kq);
+    }
+    // lane L < RPW packs the planar masks of local row L = 2i + h from the
+    // warp-uniform ballots of load i: P0 = M0 | M1 << 16 (row 2i: low halves,
+    // row 2i+1: high halves), P1 = M2 | M3 << 16
+    const int my_i = (lane >> 1) & (NL - 1);
+    const uint32_t my_sel = (lane & 1) ? 0x7632u : 0x5410u;
     uint32_t dirty = (1u << NA) - 1u;
-    int j = 0;
+    int j = 0, s = 0, sa = 0;
+    uint32_t ps = 0u, pa = 0u;  // phase parities of the current staging / A slot
     bool ok = true;
     for (int g = 0; g < groups && ok; ++g) {
       const int tg = min(G, tiles - g * G);
       for (int kc = 0; kc < nk && ok; ++kc) {
         for (int t = 0; t < tg; ++t) {
-          const int s = j % NS, sa = j % NA;
-          if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-          if (j >= NA && !(ok = mbar_wait(&a_empty[sa], ((j / NA) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          if (!(ok = mbar_wait(&stg_full[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          if (j >= NA && !(ok = mbar_wait(&a_empty[sa], pa ^ 1u, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
           const int64_t row0 = r_begin + (int64_t)(g * G + t) * tc::kRows;
           const int nrows = (int)min64(tc::kRows, r_end - row0);
-          constexpr int RPW = tc::kRows / tc::kConvWarps;  // rows per converter warp
-          constexpr int NL = RPW / 2;                       // float4 loads per lane
+          const unsigned char* st = stg + s * tc::kStgBytes;
           uint4 v[NL];  // raw fp32 bits
+          if (nrows == tc::kRows) {
 #pragma unroll
-          for (int i = 0; i < NL; ++i) {
-            const int rl = cw * RPW + 2 * i + half;
-            v[i] = (rl < nrows) ? *reinterpret_cast<const uint4*>(stg + s * tc::kStgBytes + rl * 256 + kq * 4)
-                                : make_uint4(0u, 0u, 0u, 0u);
+            for (int i = 0; i < NL; ++i) v[i] = *reinterpret_cast<const uint4*>(st + soff[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < NL; ++i)
+              v[i] = (rls[i] < nrows) ? *reinterpret_cast<const uint4*>(st + soff[i]) : make_uint4(0u, 0u, 0u, 0u);
           }
-          // Fast path: a non-negative finite value whose low 16 bits are zero is
-          // exactly its upper half in bf16 (spikes 0/1 always are), so the A
-          // operand is two byte permutes per 4 values.  Anything else (low
-          // bits set, negative incl. -0, Inf/NaN: unsigned bits >= 0x7f800000)
+          // Fast path: a non-negative value whose low 16 bits are zero is exactly
+          // its upper half in bf16 (spikes 0/1 always are), so the A operand is
+          // two byte permutes per 4 values.  One OR over the raw bits screens the
+          // slot: a sign bit, low bits or an all-ones exponent field (Inf/NaN; the
+          // OR of two other exponents can also give it, which only costs speed)
           // sends the warp down the exact path below.
-          uint32_t bits_or = 0u, bits_max = 0u;
+          uint32_t bits_or = 0u;
           bool nonunit = false;
-          uint32_t keep0 = 0u, keep1 = 0u;  // lane L (< 16) ends with the planar spike mask of local row L
+          uint32_t m[NL][4];  // ballots (warp-uniform)
           unsigned char* ahi = a_hi + sa * tc::kABytes;
 #pragma unroll
           for (int i = 0; i < NL; ++i) {
-            const int rl = cw * RPW + 2 * i + half;
             const uint4 b = v[i];
             bits_or |= b.x | b.y | b.z | b.w;
-            bits_max = max(bits_max, max(max(b.x, b.y), max(b.z, b.w)));
-            *reinterpret_cast<uint2*>(ahi + sw128_offset_bf16((uint32_t)rl, (uint32_t)kq)) =
-                make_uint2(__byte_perm(b.x, b.y, 0x7632), __byte_perm(b.z, b.w, 0x7632));
+            *reinterpret_cast<uint2*>(ahi + aoff[i]) = make_uint2(__byte_perm(b.x, b.y, 0x7632), __byte_perm(b.z, b.w, 0x7632));
             if (check_unit) {
               nonunit |= (b.x != 0u && b.x != 0x3f800000u) || (b.y != 0u && b.y != 0x3f800000u) ||
                          (b.z != 0u && b.z != 0x3f800000u) || (b.w != 0u && b.w != 0x3f800000u);
             }
             if (emit) {
-              // Planar spike masks: ballot e has bit m of lanes 0-15 = column 4m+e of
-              // row 2i, of lanes 16-31 = column 4m+e of row 2i+1.  Per row and
-              // 64-column chunk, the 4 16-bit planes are packed into 2 words
-              // (P0 = M0 | M1 << 16, P1 = M2 | M3 << 16); the CSR scan converts
-              // them to column order when it loads them.
-              const uint32_t m0 = __ballot_sync(0xffffffffu, __uint_as_float(b.x) > 0.0f);
-              const uint32_t m1 = __ballot_sync(0xffffffffu, __uint_as_float(b.y) > 0.0f);
-              const uint32_t m2 = __ballot_sync(0xffffffffu, __uint_as_float(b.z) > 0.0f);
-              const uint32_t m3 = __ballot_sync(0xffffffffu, __uint_as_float(b.w) > 0.0f);
-              if (lane == 2 * i) {
-                keep0 = __byte_perm(m0, m1, 0x5410);
-                keep1 = __byte_perm(m2, m3, 0x5410);
-              } else if (lane == 2 * i + 1) {
-                keep0 = __byte_perm(m0, m1, 0x7632);
-                keep1 = __byte_perm(m2, m3, 0x7632);
-              }
+              // ballot e: bit m of lanes 0-15 = column 4m+e of row 2i, of lanes
+              // 16-31 = column 4m+e of row 2i+1
+              m[i][0] = __ballot_sync(0xffffffffu, __uint_as_float(b.x) > 0.0f);
+              m[i][1] = __ballot_sync(0xffffffffu, __uint_as_float(b.y) > 0.0f);
+              m[i][2] = __ballot_sync(0xffffffffu, __uint_as_float(b.z) > 0.0f);
+              m[i][3] = __ballot_sync(0xffffffffu, __uint_as_float(b.w) > 0.0f);
             }
           }
           // The staging slot is released only now: every lane has stored values
@@ -325,9 +330,21 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           // that a lane had not read yet).
           __syncwarp();
           if (lane == 0) mbar_arrive(&stg_empty[s]);
-          if (emit && lane < RPW) {
+          if (emit) {
+            // Planar spike masks per row and 64-column chunk: the 4 16-bit planes
+            // packed into 2 words; the CSR pass converts them to column order.
+            uint32_t q[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t x = m[0][e];
+#pragma unroll
+              for (int i = 1; i < NL; ++i) x = (my_i == i) ? m[i][e] : x;
+              q[e] = x;
+            }
+            const uint32_t keep0 = __byte_perm(q[0], q[1], my_sel);
+            const uint32_t keep1 = __byte_perm(q[2], q[3], my_sel);
             const int rl = cw * RPW + lane;
-            if (rl < nrows) {
+            if (lane < RPW && rl < nrows) {
               const int64_t grow = row0 + rl;
               const int idx = t * tc::kRows + rl;
               const int c = __popc(keep0) + __popc(keep1);
@@ -336,26 +353,24 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
               *reinterpret_cast<uint2*>(a.bitmap + grow * a.KWP + 2 * kc) = make_uint2(keep0, keep1);
               if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = total;
             }
-          }
-          if (emit && kc == nk - 1 && a.blk_sum) {
-            // the warp's 8 rows lie in one 128-row block: one atomic per warp and level
-            const int rl = cw * RPW + lane;
-            int v = (lane < RPW && rl < nrows) ? row_count[t * tc::kRows + rl] : 0;
+            if (kc == nk - 1 && a.blk_sum) {
+              // the warp's 8 rows lie in one 128-row block: one atomic per warp and level
+              int v = (lane < RPW && rl < nrows) ? row_count[t * tc::kRows + rl] : 0;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            const int64_t g0 = row0 + cw * RPW;
-            if (lane == 0 && cw * RPW < nrows && v) {
-              atomicAdd(&a.blk_sum[g0 >> 7], v);
-              atomicAdd(&a.sup_sum[g0 >> 14], (unsigned long long)v);
+              for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+              const int64_t g0 = row0 + cw * RPW;
+              if (lane == 0 && cw * RPW < nrows && v) {
+                atomicAdd(&a.blk_sum[g0 >> 7], v);
+                atomicAdd(&a.sup_sum[g0 >> 14], (unsigned long long)v);
+              }
             }
           }
-          const bool warp_lo = __any_sync(0xffffffffu, (bits_or & 0xffffu) != 0u || bits_max >= 0x7f800000u);
+          const bool warp_lo =
+              __any_sync(0xffffffffu, (bits_or & 0x8000ffffu) != 0u || (bits_or & 0x7f800000u) == 0x7f800000u);
           if (warp_lo || ((dirty >> sa) & 1u)) {
             unsigned char* alo = a_lo + sa * tc::kABytes;
 #pragma unroll
             for (int i = 0; i < NL; ++i) {
-              const int rl = cw * RPW + 2 * i + half;
-              const uint32_t off = sw128_offset_bf16((uint32_t)rl, (uint32_t)kq);
               uint2 lo_pk = make_uint2(0u, 0u);
               if (warp_lo) {  // exact path: predicate, round-to-nearest hi, lo remainder
                 const float x[4] = {__uint_as_float(v[i].x), __uint_as_float(v[i].y), __uint_as_float(v[i].z),
@@ -363,10 +378,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                 __nv_bfloat16 h[4], l[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) split_bf16(x[e] > 0.0f ? x[e] : 0.0f, h[e], l[e]);
-                *reinterpret_cast<uint2*>(ahi + off) = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+                *reinterpret_cast<uint2*>(ahi + aoff[i]) =
+                    make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
                 lo_pk = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
               }
-              *reinterpret_cast<uint2*>(alo + off) = lo_pk;
+              *reinterpret_cast<uint2*>(alo + aoff[i]) = lo_pk;
             }
             dirty = warp_lo ? (dirty | (1u << sa)) : (dirty & ~(1u << sa));
           }
@@ -376,6 +392,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[sa]);
           ++j;
+          if (++s == NS) { s = 0; ps ^= 1u; }
+          if (++sa == NA) { sa = 0; pa ^= 1u; }
         }
       }
     }
