@@ -33,6 +33,8 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from spikestack_lite_b200.dist import RankGroup, shard_bounds  # noqa: E402
+
 METRIC = "tokens/s full-model fwd & spike-linear GSOP/s (% HBM roofline) at 1/2/4/8 B200"
 L2_BYTES = 126 * 1024 * 1024
 
@@ -117,45 +119,6 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
                 "samples": len(mhz)}
-
-
-class Dist:
-    def __init__(self):
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = False
-
-    def init(self, backend="nccl"):
-        if self.world > 1:
-            import datetime
-
-            import torch.distributed as dist
-
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local) if backend == "nccl" else None)
-            self.pg = True
-
-    def barrier(self):
-        if self.pg:
-            import torch.distributed as dist
-
-            dist.barrier()
-
-    def max(self, x):
-        if not self.pg:
-            return x
-        import torch.distributed as dist
-
-        t = torch.tensor([x], dtype=torch.float64, device=torch.device("cuda", self.local))
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def close(self):
-        if self.pg:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
 
 
 # ------------------------------------------------------------- spike-linear
@@ -448,22 +411,15 @@ def run_model(args, dist, cfg):
     torch.manual_seed(0)
     model = SpikingTransformer(**cfg["model"]).to(dev).eval()
     B = cfg["batch"]
-    per = B // dist.world
+    lo, hi = shard_bounds(B, dist.rank, dist.world)
     g = torch.Generator().manual_seed(1)
     x_all = torch.randn(B, cfg["model"]["seq_len"], cfg["model"]["input_dim"], generator=g)
-    x = x_all[dist.rank * per:(dist.rank + 1) * per].to(dev)
-    chunk = cfg.get("chunk", per)
+    x = x_all[lo:hi].to(dev)  # this rank's samples, resident before timing
+    chunk = min(cfg.get("chunk", hi - lo), hi - lo)
 
     def fwd():
-        outs = [model(x[i:i + chunk]) for i in range(0, per, chunk)]
-        logits = torch.cat(outs)
-        if dist.pg:
-            import torch.distributed as tdist
-
-            full = torch.empty(B, logits.shape[1], device=dev)
-            tdist.all_gather_into_tensor(full, logits.contiguous())
-            return full
-        return logits
+        local = torch.cat([model(x[i:i + chunk]) for i in range(0, hi - lo, chunk)])
+        return dist.gather_rows(local)  # NCCL all-gather of the logits: the only collective
 
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -528,7 +484,7 @@ def main():
     if args.batch is not None and "B" in cfg:
         cfg["B"] = args.batch
         cfg["name"] += f" (B overridden to {args.batch})"
-    dist = Dist()
+    dist = RankGroup("nccl")
 
     if args.impl == "reference":
         if dist.rank != 0:
@@ -540,7 +496,7 @@ def main():
         print(json.dumps(run_reference_spike_linear(args, dist, cfg)), flush=True)
         return
 
-    dist.init("nccl")
+    dist.init()
     try:
         if args.workload in ("spike_linear", "sweep"):
             res = run_spike_linear(args, dist, cfg)

@@ -28,7 +28,7 @@
 // producer, warp 1 TMEM owner + MMA issuer, warps 2-9 converters, warps
 // 10-13 epilogue.  Every wait is bounded (2 s) and reports
 // SPK_DEV_PIPE_TIMEOUT; issued copies and MMAs are drained before exit and
-// TMEM is always freed.  No multicast anywhere.
+// TMEM is always freed.  Every copy lands in this CTA's own shared memory.
 #include "tma.cuh"
 
 namespace spk {

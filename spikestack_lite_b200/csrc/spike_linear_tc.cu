@@ -20,7 +20,7 @@
 //   warp 0     TMA producer: S tiles via a 2-D tensor map (fp32, 32-row x
 //              64-column boxes, zero fill past the tensor edge) into a 3-slot
 //              staging ring; weight chunks of the pre-split image by 1-D bulk
-//              copy.  No multicast anywhere.
+//              copy.  Every copy lands in this CTA's own shared memory.
 //   warp 1     TMEM owner and MMA issuer (one thread).
 //   warps 2-17 converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
 //              128-byte-swizzled K-major A layout; optionally the packed spike

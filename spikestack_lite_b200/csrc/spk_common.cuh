@@ -3,7 +3,7 @@
 // Host side: status codes and the thread-local last-error string that every
 // extern "C" entry point reports through (see include/spikestack_b200.h).
 // Device side: thin inline-PTX wrappers for the sm_100a features the kernels
-// use -- mbarriers, 1-D bulk copies (cp.async.bulk, never with multicast),
+// use -- mbarriers, 1-D bulk copies (cp.async.bulk into this CTA only),
 // tcgen05 (TMEM alloc / MMA / commit / ld) and the UMMA shared-memory and
 // instruction descriptors.  Every spin-wait is bounded by wall-clock time and
 // reports a device error code instead of hanging.
@@ -150,7 +150,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// ---- 1-D bulk copy global -> shared (no multicast), completes on an mbarrier
+// ---- 1-D bulk copy global -> this CTA's shared memory, completes on an mbarrier
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

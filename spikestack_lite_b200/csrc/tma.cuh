@@ -1,5 +1,5 @@
 // Tensor-memory-accelerator helpers shared by the tcgen05 kernels: the 2-D
-// tiled load (never with cluster multicast) and host-side encoding of fp32
+// tiled load into this CTA's own shared memory and host-side encoding of fp32
 // row-major tensor maps through the driver entry point.
 #pragma once
 
