@@ -221,7 +221,21 @@ def run_spike_linear(args, dist, cfg):
                             if cfg["csr"] else 0)
     dom = "dense" if kernel_ms.get("dense") else "spmm_csr"
     dom_ms = kernel_ms.get(dom)
-    achieved = alg_dense / (dom_ms / 1e3) / 1e9 if dom_ms else None
+    # bound of the dominant kernel: HBM bytes vs dense tensor FLOPs (counted once,
+    # whatever the operand split multiplies them into)
+    flops = 2.0 * T * M * K * N
+    tensor_bound = dom == "dense" and flops / (pk["bf16_tflops"] * 1e12) > alg_dense / (pk["hbm_gbs"] * 1e9)
+    if tensor_bound:
+        achieved = flops / (dom_ms / 1e3) / 1e12 if dom_ms else None
+        roof = {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None, "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4) if achieved else None,
+                "alg_flops_per_launch": flops, "traffic": None}
+    else:
+        achieved = alg_dense / (dom_ms / 1e3) / 1e9 if dom_ms else None
+        roof = {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4) if achieved else None,
+                "alg_bytes_per_launch": int(alg_dense),
+                "traffic": profile_traffic(cfg["traffic_profile"]) if cfg.get("traffic_profile") else None}
     step_ms = ms_max / args.steps
     res = {
         "metric": METRIC, "value": round(value, 2), "unit": "GSOP/s", "n_gpus": dist.world, "steps": args.steps,
@@ -234,11 +248,8 @@ def run_spike_linear(args, dist, cfg):
         "step_gbs": round(alg_step / (step_ms / 1e3) / 1e9, 1),
         "step_hbm_frac": round(alg_step / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
         "kernel_ms": {k: round(v, 5) for k, v in kernel_ms.items()},
-        "roofline": {"kernel": "spike_linear_tc_kernel" if dom == "dense" else "spmm_csr_kernel", "bound": "hbm",
-                     "achieved": round(achieved, 1) if achieved else None, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4) if achieved else None,
-                     "peak_src": pk["src"], "alg_bytes_per_launch": int(alg_dense),
-                     "traffic": profile_traffic("spike_linear_dense_c2")},
+        "roofline": {"kernel": ("spike_linear_tf32_kernel" if cfg["w_dtype"] == "f32" else "spike_linear_tc_kernel")
+                     if dom == "dense" else "spmm_csr_kernel", **roof, "peak_src": pk["src"]},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "parity_rel_err": parity,
         "clocks": clocks.summary(),
@@ -481,6 +492,8 @@ def main():
     if args.rows is not None:
         cfg["M"] = args.rows
         cfg["name"] += f" (M overridden to {args.rows})"
+    if args.workload == "spike_linear" and args.rows is None and args.p is None:
+        cfg["traffic_profile"] = "spike_linear_dense_c2"  # the ncu capture of this exact configuration
     if args.batch is not None and "B" in cfg:
         cfg["B"] = args.batch
         cfg["name"] += f" (B overridden to {args.batch})"

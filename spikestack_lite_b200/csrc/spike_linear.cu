@@ -2,7 +2,8 @@
 // two reference-compatible ops (sparse_forward / sparse_multistep_forward).
 //
 // Orchestration per call (one stream, no host synchronisation):
-//   dense branch:  W image (bf16 hi/lo, pre-swizzled)  ->  tcgen05 kernel
+//   dense branch:  W image (tf32 hi/lo for fp32 W, bf16 for bf16 W; pre-
+//                  swizzled)  ->  tcgen05 kernel
 //                  [-> CSR scan when CSR outputs are requested]
 //   CSR branch:    CSR scan of all planes  ->  CSR SpMM with the weight tile
 //                  held in shared memory across all planes
@@ -45,7 +46,10 @@ inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool inte
   off += align_up(sizeof(uint64_t) * (size_t)ceil_div((int64_t)T * M, 16384), 256);
   L.zero_end = off;
   L.img = off;
-  off += align_up(tc_plan(K, N, w_dtype).img_bytes, 1024);
+  {
+    const TcPlan p = tc_plan(K, N, w_dtype);
+    off += align_up(w_dtype == SPK_F32 ? tf32_img_bytes(p) : p.img_bytes, 1024);
+  }
   L.bitmap = off;
   off += align_up(sizeof(uint32_t) * (size_t)T * M * (2 * ((K + 63) / 64)), 256);  // planar masks
   L.row_cnt = off;
@@ -90,8 +94,12 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
     const TcPlan p = tc_plan(K, N, w_dtype);
     unsigned char* img = reinterpret_cast<unsigned char*>(wsb + L.img);
     uint32_t* state = reinterpret_cast<uint32_t*>(wsb + L.csr_state);
-    rc = launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr,
-                        want_csr ? (int64_t)((L.zero_end - L.csr_state) / 4) : 0, stream);
+    const int64_t zero_words = want_csr ? (int64_t)((L.zero_end - L.csr_state) / 4) : 0;
+    // fp32 W: tf32 kernel (spikes read by the tensor cores straight from the
+    // TMA staging); bf16 W: bf16 kernel (one MMA per k-step, no W split)
+    const bool tf32 = w_dtype == SPK_F32;
+    rc = tf32 ? launch_w_image_tf32(W, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream)
+              : launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream);
     if (rc) return rc;
     TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
     if (want_csr) {
@@ -102,7 +110,8 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
       // value check only when CSR values are requested (spikes of 1 need no gather)
       if (values) o.nonunit = reinterpret_cast<int*>(wsb + L.csr_state) + 1;  // ScanState::nonunit
     }
-    rc = launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
+    rc = tf32 ? launch_tf32(S, (int64_t)T * M, K, N, p, img, o, stream)
+              : launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
     if (rc) return rc;
     if (want_csr) {
       rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, o.blk_sum, o.sup_sum, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,

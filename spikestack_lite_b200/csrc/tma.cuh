@@ -58,4 +58,26 @@ inline int make_map_2d_f32(CUtensorMap* map, const float* base, int64_t rows, in
   return SPK_OK;
 }
 
+// As make_map_2d_f32 with the 128-byte swizzle: box_cols * 4 must be 128, and
+// each box lands as 128-byte rows in 1024-byte atoms with the 16-byte chunks
+// of row r XOR-permuted by r & 7 -- the K-major UMMA operand layout.
+inline int make_map_2d_swizzled_f32(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t pitch,
+                                    int box_cols, int box_rows, const char* what) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(SPK_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch * 4) % 16 != 0 || box_cols * 4 != 128)
+    return fail(SPK_EINVAL, "%s: base 16-byte aligned, row pitch a multiple of 16 bytes, 32-column boxes", what);
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)pitch * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SPK_ECUDA, "cuTensorMapEncodeTiled (swizzled) failed (%d) for %s [%lld, %lld]", (int)r, what,
+                (long long)rows, (long long)cols);
+  return SPK_OK;
+}
+
 }  // namespace spk
