@@ -223,6 +223,34 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 TMEM lanes x 256 bits, 4 (x4) or 2 (x2) repetitions along the columns:
+// thread t holds, for repetition j, columns 8j + 2(t % 4) + {0, 1} of lane
+// base + t / 4 (v[4j], v[4j+1]) and of lane base + t / 4 + 8 (v[4j+2],
+// v[4j+3]) -- four threads share a row, so row stores fill whole sectors.
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+#pragma unroll
+  for (int i = 8; i < 16; ++i) v[i] = 0.0f;
+}
+
 // UMMA shared-memory matrix descriptor for a K-major operand stored in the
 // canonical 128-byte-swizzled layout: rows of 128 bytes, 8-row groups 1024
 // bytes apart, the 16-byte chunk c of row r stored at chunk (c ^ (r & 7)).
