@@ -339,7 +339,7 @@ __device__ __forceinline__ void prefix_from_sums(const CsrArgs& a, int64_t r0, i
 // CSR from the dense kernel's planar spike masks (row counts and block sums
 // come with them): one row per lane, 128 rows per CTA.  For every 64-column
 // chunk a lane rebuilds the two column-order words from the four 16-bit
-// planes with a shared 8-bit spread table and writes the set columns in
+// planes (8-bit groups spread to every 4th bit) and writes the set columns in
 // ascending order to its row's segment.  No look-back and no waiting: every
 // prefix is a sum of counts that are complete when the grid starts.
 // Column indices of a warp's 32 rows are contiguous in col_idx: lanes expand
@@ -353,11 +353,9 @@ constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
 
 __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
   extern __shared__ __align__(16) int32_t s_buf_all[];  // [kMaskWarps][kWarpBuf]
-  __shared__ uint32_t s_spread[256];
   __shared__ int64_t s_red[2 * kMaskWarps];
   __shared__ int s_wtot[kMaskWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < 256; i += kMaskRows) s_spread[i] = spread8_stride4(i);
   // programmatic dependent of the dense kernel: its outputs are complete after this
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int plane = (int)(blockIdx.x / tiles_pp);
@@ -426,11 +424,12 @@ __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, in
       }
       if ((pw.x | pw.y) == 0u) continue;
       // column 64c + 4m + e is bit m of plane e (planes: pw.x lo/hi, pw.y lo/hi)
+        // spread arithmetically: a shared table would be read at random banks
       const uint32_t words[2] = {
-          s_spread[pw.x & 0xffu] | (s_spread[(pw.x >> 16) & 0xffu] << 1) | (s_spread[pw.y & 0xffu] << 2) |
-              (s_spread[(pw.y >> 16) & 0xffu] << 3),
-          s_spread[(pw.x >> 8) & 0xffu] | (s_spread[pw.x >> 24] << 1) | (s_spread[(pw.y >> 8) & 0xffu] << 2) |
-              (s_spread[pw.y >> 24] << 3)};
+          spread8_stride4(pw.x & 0xffu) | (spread8_stride4((pw.x >> 16) & 0xffu) << 1) |
+              (spread8_stride4(pw.y & 0xffu) << 2) | (spread8_stride4((pw.y >> 16) & 0xffu) << 3),
+          spread8_stride4((pw.x >> 8) & 0xffu) | (spread8_stride4(pw.x >> 24) << 1) |
+              (spread8_stride4((pw.y >> 8) & 0xffu) << 2) | (spread8_stride4(pw.y >> 24) << 3)};
   #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t bits = words[h];

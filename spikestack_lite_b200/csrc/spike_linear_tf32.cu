@@ -33,6 +33,8 @@ constexpr int kRows = 128;                 // MMA M: one row tile
 constexpr int kKChunk = 64;                // columns per staging slot
 constexpr int kAtomBytes = kRows * 128;    // one swizzle-atom column of a slot: 128 rows x 32 fp32 = 16 KB
 constexpr int kStgBytes = 2 * kAtomBytes;  // 32 KB
+constexpr int kBoxRows = 32;              // TMA box: 32 fp32 columns x 32 rows = 4 KB (4 swizzle atoms)
+constexpr int kBoxBytes = kBoxRows * 128;
 constexpr int kConvWarps = 16;
 constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 constexpr int kNS = 3;                     // staging slots
@@ -176,10 +178,16 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
             if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
               break;
             const int64_t row0 = r_begin + (int64_t)(g * G + t) * t32::kRows;
-            mbar_arrive_expect_tx(&stg_full[s], t32::kStgBytes);
-            tma_load_2d(stg + s * t32::kStgBytes, &tmap_s, kc * t32::kKChunk, (int)row0, &stg_full[s]);
-            tma_load_2d(stg + s * t32::kStgBytes + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, (int)row0,
-                        &stg_full[s]);
+            // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
+            // (rows a box leaves out keep stale data; the converters and the epilogue ignore them)
+            const int nbox = (int)ceil_div(min64(t32::kRows, r_end - row0), t32::kBoxRows);
+            mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(2 * nbox * t32::kBoxBytes));
+            for (int b = 0; b < nbox; ++b) {
+              unsigned char* dst = stg + s * t32::kStgBytes + b * t32::kBoxBytes;
+              const int y = (int)row0 + b * t32::kBoxRows;
+              tma_load_2d(dst, &tmap_s, kc * t32::kKChunk, y, &stg_full[s]);
+              tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
+            }
             ++j;
           }
         }
@@ -471,16 +479,16 @@ template <typename WT>
 __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk,
                                     unsigned char* img, uint32_t* zero, int64_t zero_words) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int64_t total = (int64_t)((N + NT - 1) / NT) * NT * nk * 16;  // one thread per (n, 4 k)
+  const int64_t npad = (int64_t)((N + NT - 1) / NT) * NT;
+  const int64_t total = npad * nk * 16;  // one thread per (n, 4 k); n fastest: coalesced along W rows
   const size_t atom = (size_t)NT * 128;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = tid; i < zero_words; i += nthr) zero[i] = 0u;
   for (int64_t i = tid; i < total; i += nthr) {
-    const int k4 = (int)(i % 16);        // 4-column group within the 64-wide chunk
-    const int64_t rest = i / 16;
-    const int64_t ng = rest / nk;
-    const int kc = (int)(rest % nk);
+    const int64_t ng = i % npad;
+    const int64_t kq = i / npad;         // global 4-column group
+    const int kc = (int)(kq / 16), k4 = (int)(kq % 16);
     const int t = (int)(ng / NT), nl = (int)(ng % NT);
     float h[4], l[4];
 #pragma unroll
@@ -536,7 +544,7 @@ int launch_w_image_tf32(const void* W, int64_t sk, int64_t sn, int K, int N, con
 int launch_tf32(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
                 cudaStream_t stream) {
   CUtensorMap map;
-  int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, t32::kRows, "S");
+  int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, t32::kBoxRows, "S");
   if (rc) return rc;
   TcArgs a{};
   a.R = R;
