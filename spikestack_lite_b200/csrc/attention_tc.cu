@@ -640,8 +640,11 @@ __global__ void __launch_bounds__(at::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 10-13)
+    // 16-lane x 256-bit TMEM loads: four threads per position, so every
+    // store instruction writes whole 32-byte sectors of eight output rows.
     constexpr int G = kGrp / DH;
     const int q = warp & 3;
+    const int ar = lane >> 2, cp = (lane & 3) * 2;
     int ti = 0;
     for (int64_t it = i0; it < i1; ++it) {
       const int64_t u = it / a.tiles;
@@ -649,35 +652,43 @@ __global__ void __launch_bounds__(at::kThreads, 1)
       const int ab = ti & 1;
       if (!mbar_wait(&acc_full[ab], (ti / 2) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) break;
       tc_fence_after();
-      const int pos = tile * kRows2 + 32 * q + lane;
-      const bool valid = pos < a.L;
-      const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kAcc2);
-      float dn[16];
-      tmem_ld16(tb + kGrp, dn);
-      tmem_wait_ld();
-      tmem_reg_fence(dn);
-      float inv[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) inv[h] = __frcp_rn(dn[h] + a.eps);
-      float* orow = a.out + ((u / a.groups) * a.L + pos) * (int64_t)a.d + (u % a.groups) * kGrp;
-#pragma unroll
-      for (int c0 = 0; c0 < kGrp / 16; c0 += 2) {  // unrolled: the head of a column block is static
-        float acc[2][16];
-        tmem_ld16(tb + (uint32_t)(c0 * 16), acc[0]);
-        tmem_ld16(tb + (uint32_t)((c0 + 1) * 16), acc[1]);
+      float* obase = a.out + (u / a.groups) * a.L * (int64_t)a.d + (u % a.groups) * kGrp;
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int posA = tile * kRows2 + 32 * q + 16 * h2 + ar;  // this thread's rows: posA, posA + 8
+        const uint32_t tb = tmem + ((uint32_t)(32 * q + 16 * h2) << 16) + (uint32_t)(ab * kAcc2);
+        // key-mass products (columns 128 + h) of both rows, gathered from the quad
+        float dn[16];
+        tmem_ld_16x256b_x2(tb + kGrp, dn);
         tmem_wait_ld();
-        tmem_reg_fence(acc[0]);
-        tmem_reg_fence(acc[1]);
-        if (valid) {
+        tmem_reg_fence(dn);
+        float inv[2][G];
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int cbase = (c0 + hh) * 16;
-            const float r = inv[cbase / DH];
+        for (int h = 0; h < G; ++h) {
+          // column 128 + h (h < 8) sits in quad member h / 2, element h % 2
+          const int src = (lane & ~3) | (h >> 1);
+          const float d0 = __shfl_sync(0xffffffffu, (h & 1) ? dn[1] : dn[0], src);
+          const float d1 = __shfl_sync(0xffffffffu, (h & 1) ? dn[3] : dn[2], src);
+          inv[0][h] = __frcp_rn(d0 + a.eps);
+          inv[1][h] = __frcp_rn(d1 + a.eps);
+        }
 #pragma unroll
-            for (int gq = 0; gq < 4; ++gq)
-              *reinterpret_cast<float4*>(orow + cbase + 4 * gq) =
-                  make_float4(acc[hh][4 * gq] * r, acc[hh][4 * gq + 1] * r, acc[hh][4 * gq + 2] * r,
-                              acc[hh][4 * gq + 3] * r);
+        for (int cb = 0; cb < kGrp; cb += 32) {  // unrolled: the head of each 8-column block is static
+          float v[16];
+          tmem_ld_16x256b_x4(tb + (uint32_t)cb, v);
+          tmem_wait_ld();
+          tmem_reg_fence(v);
+#pragma unroll
+          for (int jb = 0; jb < 4; ++jb) {
+            const int col = cb + 8 * jb;
+            const int hd = col / DH;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const int pos = posA + 8 * rr;
+              if (pos < a.L)
+                *reinterpret_cast<float2*>(obase + (int64_t)pos * a.d + col + cp) =
+                    make_float2(v[4 * jb + 2 * rr] * inv[rr][hd], v[4 * jb + 2 * rr + 1] * inv[rr][hd]);
+            }
           }
         }
       }
