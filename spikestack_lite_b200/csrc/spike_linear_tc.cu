@@ -25,7 +25,8 @@
 //   warps 2-17 converters: staging fp32 -> predicate -> bf16 hi [/lo] in the
 //              128-byte-swizzled K-major A layout; optionally the packed spike
 //              bitmap and per-row counts the CSR pass consumes.
-//   warps 18-21 epilogue: tcgen05.ld of their TMEM lane quarter, + bias, store Y.
+//   warps 18-21 epilogue: tcgen05.ld (16 lanes x 256 bits) of their TMEM lane
+//              quarter, + bias, sector-filling stores of Y.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; each role then
 // leaves its loop, issued copies and MMAs are drained, TMEM is freed.
 #include "tma.cuh"
@@ -399,45 +400,49 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 18-21)
+    // 16-lane x 256-bit TMEM loads: four threads per row, so every store
+    // instruction writes whole 32-byte sectors of eight rows.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ar = lane >> 2, cp = (lane & 3) * 2;
     for (int g = 0; g < groups; ++g) {
       const int tg = min(G, tiles - g * G);
       const int ab = g & 1;
       if (!mbar_wait(&acc_full[ab], (g / 2) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) break;
       tc_fence_after();
       for (int t = 0; t < tg; ++t) {
-        const int64_t row = r_begin + (int64_t)(g * G + t) * tc::kRows + q * 32 + lane;
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
 #pragma unroll 1
-        for (int c0 = 0; c0 < NT / 16; c0 += 2) {
-          float acc[2][16];
-          tmem_ld16(tbase + (uint32_t)(c0 * 16), acc[0]);
-          if (c0 + 1 < NT / 16) tmem_ld16(tbase + (uint32_t)((c0 + 1) * 16), acc[1]);
-          tmem_wait_ld();
-          tmem_reg_fence(acc[0]);
-          if (c0 + 1 < NT / 16) tmem_reg_fence(acc[1]);
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int64_t rowA = r_begin + (int64_t)(g * G + t) * tc::kRows + q * 32 + h2 * 16 + ar;
+          const int64_t rowB = rowA + 8;
+          const uint32_t tb = tmem + ((uint32_t)(q * 32 + h2 * 16) << 16) +
+                              (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
+#pragma unroll 1
+          for (int cb = 0; cb < NT; cb += 32) {
+            float v[16];
+            if (cb + 32 <= NT) tmem_ld_16x256b_x4(tb + (uint32_t)cb, v);
+            else tmem_ld_16x256b_x2(tb + (uint32_t)cb, v);
+            tmem_wait_ld();
+            tmem_reg_fence(v);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = c0 + h;
-            const int n = n0 + c * 16;
-            if (c < NT / 16 && row < r_end) {
-              float* y = a.Y + row * a.N + n;
-              if (a.y_vec && n + 16 <= a.N) {
+            for (int jb = 0; jb < 4; ++jb) {
+              const int n = n0 + cb + 8 * jb + cp;
+              if (cb + 8 * jb >= NT) break;
 #pragma unroll
-                for (int gq = 0; gq < 4; ++gq) {
-                  float4 o = make_float4(acc[h][4 * gq], acc[h][4 * gq + 1], acc[h][4 * gq + 2], acc[h][4 * gq + 3]);
+              for (int rr = 0; rr < 2; ++rr) {
+                const int64_t row = rr ? rowB : rowA;
+                if (row >= r_end) continue;
+                float x0 = v[4 * jb + 2 * rr], x1 = v[4 * jb + 2 * rr + 1];
+                float* y = a.Y + row * a.N + n;
+                if (a.y_vec && n + 2 <= a.N) {
                   if (a.bias) {
-                    o.x += a.bias[n + 4 * gq];
-                    o.y += a.bias[n + 4 * gq + 1];
-                    o.z += a.bias[n + 4 * gq + 2];
-                    o.w += a.bias[n + 4 * gq + 3];
+                    x0 += a.bias[n];
+                    x1 += a.bias[n + 1];
                   }
-                  *reinterpret_cast<float4*>(y + 4 * gq) = o;
+                  *reinterpret_cast<float2*>(y) = make_float2(x0, x1);
+                } else {
+                  if (n < a.N) y[0] = a.bias ? x0 + a.bias[n] : x0;
+                  if (n + 1 < a.N) y[1] = a.bias ? x1 + a.bias[n + 1] : x1;
                 }
-              } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                  if (n + e < a.N) y[e] = a.bias ? acc[h][e] + a.bias[n + e] : acc[h][e];
               }
             }
           }
