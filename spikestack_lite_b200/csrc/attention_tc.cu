@@ -106,8 +106,7 @@ __global__ void __launch_bounds__(at::kThreads, 1)
   using namespace at;
   constexpr int G = kGrp / DH;  // heads per group
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;
   unsigned char* ops = stg + kNS1 * kStg1;
   float* km_part = reinterpret_cast<float*>(ops + kNA1 * 4 * kOp1);  // [2][kConvWarps][128], 16-byte aligned
@@ -431,8 +430,7 @@ __global__ void __launch_bounds__(at::kThreads, 1)
     attn_out_tc_kernel(const __grid_constant__ CUtensorMap tm_q, AttnOutArgs a) {
   using namespace at;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* bimg = base;                        // [hi | lo][2 K chunks][144 rows x 128 B]
   unsigned char* stg = bimg + kImgBytes;             // [kNS2][32 KB]
   unsigned char* a_hi = stg + kNS2 * kStg2;          // [kNA2][16 KB]

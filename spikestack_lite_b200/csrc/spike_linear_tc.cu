@@ -93,8 +93,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   using C = tc::Cfg<NT, WSPLIT>;
   constexpr int G = C::kG, NS = tc::kNS, NA = tc::kNA, NB = tc::kNB;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                     // [NS][32 KB] fp32 staging
   unsigned char* a_hi = stg + NS * tc::kStgBytes;                // [NA][16 KB]
   unsigned char* a_lo = a_hi + NA * tc::kABytes;                 // [NA][16 KB]

@@ -39,6 +39,7 @@ constexpr int kConvWarps = 16;
 constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 constexpr int kNS = 3;                     // staging slots
 constexpr int kNB = 2;                     // weight chunk slots
+constexpr int kPrefetch = 4;               // slots of S prefetched into L2 ahead of the ring
 
 template <int NT>
 struct Cfg {
@@ -96,8 +97,7 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
   using C = t32::Cfg<NT>;
   constexpr int G = C::kG, NS = t32::kNS, NB = t32::kNB, CW = t32::kConvWarps;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                   // [NS][2 atoms x 16 KB] fp32 staging = A operand
   unsigned char* bst = stg + NS * t32::kStgBytes;               // [NB][hi 2 atoms | lo 2 atoms]
   uint64_t* bars = reinterpret_cast<uint64_t*>(bst + NB * C::kBBytes);
@@ -161,6 +161,26 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_map(&tmap_s);
+      // L2 prefetch of the slots kPrefetch ahead: the staging ring holds only
+      // three slots, so their refills should come from L2, not HBM
+      int pg = 0, pkc = 0, pt = 0;
+      auto prefetch_next = [&]() {
+        if (pg >= groups) return;
+        const int64_t prow = r_begin + (int64_t)(pg * G + pt) * t32::kRows;
+        const int pbox = (int)ceil_div(min64(t32::kRows, r_end - prow), t32::kBoxRows);
+        for (int b = 0; b < pbox; ++b) {
+          tma_prefetch_l2_2d(&tmap_s, pkc * t32::kKChunk, (int)prow + b * t32::kBoxRows);
+          tma_prefetch_l2_2d(&tmap_s, pkc * t32::kKChunk + 32, (int)prow + b * t32::kBoxRows);
+        }
+        if (++pt == min(G, tiles - pg * G)) {
+          pt = 0;
+          if (++pkc == nk) {
+            pkc = 0;
+            ++pg;
+          }
+        }
+      };
+      for (int i = 0; i < t32::kPrefetch; ++i) prefetch_next();
       int j = 0, jb = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
@@ -188,6 +208,7 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
               tma_load_2d(dst, &tmap_s, kc * t32::kKChunk, y, &stg_full[s]);
               tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
             }
+            prefetch_next();
             ++j;
           }
         }

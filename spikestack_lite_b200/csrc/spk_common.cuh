@@ -102,6 +102,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void report_device_error(int code) { atomicOr(&g_device_error, code); }
 
+// First 1024-byte-aligned byte of a dynamic shared array.  Offsetting the
+// __shared__ array itself (rather than rounding an integer address) keeps the
+// pointer in the shared state space, so accesses through it compile to
+// shared-memory loads and stores instead of generic ones.
+__device__ __forceinline__ unsigned char* smem_aligned_1024(unsigned char* smem) {
+  return smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
+}
+
 // ---- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
