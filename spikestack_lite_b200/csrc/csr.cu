@@ -346,12 +346,20 @@ __device__ __forceinline__ void prefix_from_sums(const CsrArgs& a, int64_t r0, i
 // into a per-warp shared buffer and the warp copies it out with coalesced
 // stores (a warp whose rows hold more than kWarpBuf spikes, or whose values
 // are requested, writes straight to global memory).
-constexpr int kMaskRows = 128;
-constexpr int kMaskWarps = kMaskRows / 32;
-constexpr int kWarpBuf = 2048;
+// Two lanes per row, each taking half of the row's 64-column chunks: the lanes
+// are ordered (row, half), so one warp-wide scan of the half counts gives every
+// half its first slot, and each lane's serial expansion is half a row long.
+// A warp's 16 rows are contiguous in col_idx: lanes expand into a per-warp
+// shared buffer and the warp copies it out with coalesced stores (a warp whose
+// rows hold more than kWarpBuf spikes, or whose values are requested, writes
+// straight to global memory).
+constexpr int kMaskRows = 128;                 // rows per CTA
+constexpr int kMaskThreads = 2 * kMaskRows;     // two lanes per row, each half of the row's chunks
+constexpr int kMaskWarps = kMaskThreads / 32;
+constexpr int kWarpBuf = 1024;                  // column slots staged per warp (16 rows)
 constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
 
-__global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
+__global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
   extern __shared__ __align__(16) int32_t s_buf_all[];  // [kMaskWarps][kWarpBuf]
   __shared__ int64_t s_red[2 * kMaskWarps];
   __shared__ int s_wtot[kMaskWarps];
@@ -361,19 +369,27 @@ __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, in
   const int plane = (int)(blockIdx.x / tiles_pp);
   const int64_t row0 = (blockIdx.x % tiles_pp) * kMaskRows;  // row within the plane
   const int64_t grow0 = (int64_t)plane * a.M + row0;
-  const int64_t r = row0 + threadIdx.x;
+  const int rl = warp * 16 + (lane >> 1), hf = lane & 1;  // row in the CTA, half of its chunks
+  const int64_t r = row0 + rl;
   const bool valid = r < a.M;
-  const int64_t grow = grow0 + threadIdx.x;
-  const int cnt = valid ? a.row_cnt[grow] : 0;
-  const int nch = a.KWP / 2;
+  const int64_t grow = grow0 + rl;
+  const int nch = a.KWP / 2, nh0 = (nch + 1) / 2;
+  const int c0 = hf ? nh0 : 0, c1 = hf ? nch : nh0;
   const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow * a.KWP);
-  constexpr int kPre = 8;  // mask chunks fetched ahead of the prefix computation
+  constexpr int kPre = 4;  // mask chunks fetched ahead of the prefix computation
   uint2 pre_w[kPre];
+  int cnt = 0;            // spikes in this half of the row
 #pragma unroll
-  for (int c = 0; c < kPre; ++c) pre_w[c] = (cnt > 0 && c < nch) ? __ldg(src + c) : make_uint2(0u, 0u);
+  for (int c = 0; c < kPre; ++c) {
+    pre_w[c] = (valid && c0 + c < c1) ? __ldg(src + c0 + c) : make_uint2(0u, 0u);
+    cnt += __popc(pre_w[c].x) + __popc(pre_w[c].y);
+  }
+  for (int c = c0 + kPre; valid && c < c1; ++c) {
+    const uint2 pw = __ldg(src + c);
+    cnt += __popc(pw.x) + __popc(pw.y);
+  }
   int64_t pre_tile, pre_plane;
   prefix_from_sums(a, grow0, (int64_t)plane * a.M, s_red, pre_tile, pre_plane);
-  // exclusive prefix of the row counts inside the CTA
   int incl = cnt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -388,11 +404,12 @@ __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, in
     wbase += (w < warp) ? s_wtot[w] : 0;
     ctot += s_wtot[w];
   }
-  const int64_t pos = pre_tile + wbase + incl - cnt;  // first slot of this row in col_idx
+  const int64_t pos = pre_tile + wbase + incl - cnt;
   const int64_t rel = pre_tile - pre_plane;
-  if (valid) {
+  const int cnt_row = cnt + __shfl_xor_sync(0xffffffffu, cnt, 1);  // both halves
+  if (valid && hf == 1) {
     a.row_ptr[(int64_t)plane * (a.M + 1) + r + 1] = (int32_t)(rel + wbase + incl);
-    if (a.nnz_row) a.nnz_row[grow] = cnt;
+    if (a.nnz_row) a.nnz_row[grow] = cnt_row;
   }
   if (threadIdx.x == 0) {
     if (row0 == 0) {
@@ -413,36 +430,35 @@ __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, in
     float* vdst = a.values ? a.values + (fits ? pos : 0) : nullptr;
     int k = 0;
     bool overflow = false;
-    for (int c = 0; c < nch; ++c) {
+    for (int c = c0; c < c1; ++c) {
       uint2 pw;
-      if (c < kPre) {
+      if (c - c0 < kPre) {
 #pragma unroll
         for (int e = 0; e < kPre; ++e)
-          if (e == c) pw = pre_w[e];
+          if (e == c - c0) pw = pre_w[e];
       } else {
         pw = __ldg(src + c);
       }
       if ((pw.x | pw.y) == 0u) continue;
       // column 64c + 4m + e is bit m of plane e (planes: pw.x lo/hi, pw.y lo/hi)
-        // spread arithmetically: a shared table would be read at random banks
       const uint32_t words[2] = {
           spread8_stride4(pw.x & 0xffu) | (spread8_stride4((pw.x >> 16) & 0xffu) << 1) |
               (spread8_stride4(pw.y & 0xffu) << 2) | (spread8_stride4((pw.y >> 16) & 0xffu) << 3),
           spread8_stride4((pw.x >> 8) & 0xffu) | (spread8_stride4(pw.x >> 24) << 1) |
               (spread8_stride4((pw.y >> 8) & 0xffu) << 2) | (spread8_stride4(pw.y >> 24) << 3)};
-  #pragma unroll
+#pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t bits = words[h];
-        const int base = 64 * c + 32 * h;
+        const int cb = 64 * c + 32 * h;
         if (fits) {
           if (vdst == nullptr) {
             while (bits) {
-              dst[k++] = base + __ffs(bits) - 1;
+              dst[k++] = cb + __ffs(bits) - 1;
               bits &= bits - 1u;
             }
           } else {
             while (bits) {
-              const int col = base + __ffs(bits) - 1;
+              const int col = cb + __ffs(bits) - 1;
               bits &= bits - 1u;
               dst[k] = col;
               vdst[k++] = unit_values ? 1.0f : row[col];
@@ -450,7 +466,7 @@ __global__ void __launch_bounds__(kMaskRows) csr_from_masks_kernel(CsrArgs a, in
           }
         } else {
           while (bits) {
-            const int col = base + __ffs(bits) - 1;
+            const int col = cb + __ffs(bits) - 1;
             bits &= bits - 1u;
             const int64_t p = pos + k++;
             if (p < a.col_capacity) {
@@ -509,7 +525,7 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
     prof_before(SPK_KERNEL_CSR_SCAN, stream);
     SPK_CUDA_TRY(cudaFuncSetAttribute(csr_from_masks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kMaskSmem));
-    SPK_CUDA_TRY(launch_dependent(csr_from_masks_kernel, dim3((unsigned)(tpp * T)), dim3(kMaskRows), kMaskSmem,
+    SPK_CUDA_TRY(launch_dependent(csr_from_masks_kernel, dim3((unsigned)(tpp * T)), dim3(kMaskThreads), kMaskSmem,
                                   stream, a, tpp));
     prof_after(SPK_KERNEL_CSR_SCAN, stream);
     SPK_LAUNCH_CHECK();

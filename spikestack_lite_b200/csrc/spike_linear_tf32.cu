@@ -39,7 +39,6 @@ constexpr int kConvWarps = 16;
 constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 constexpr int kNS = 3;                     // staging slots
 constexpr int kNB = 2;                     // weight chunk slots
-constexpr int kPrefetch = 4;               // slots of S prefetched into L2 ahead of the ring
 
 template <int NT>
 struct Cfg {
@@ -161,26 +160,6 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_map(&tmap_s);
-      // L2 prefetch of the slots kPrefetch ahead: the staging ring holds only
-      // three slots, so their refills should come from L2, not HBM
-      int pg = 0, pkc = 0, pt = 0;
-      auto prefetch_next = [&]() {
-        if (pg >= groups) return;
-        const int64_t prow = r_begin + (int64_t)(pg * G + pt) * t32::kRows;
-        const int pbox = (int)ceil_div(min64(t32::kRows, r_end - prow), t32::kBoxRows);
-        for (int b = 0; b < pbox; ++b) {
-          tma_prefetch_l2_2d(&tmap_s, pkc * t32::kKChunk, (int)prow + b * t32::kBoxRows);
-          tma_prefetch_l2_2d(&tmap_s, pkc * t32::kKChunk + 32, (int)prow + b * t32::kBoxRows);
-        }
-        if (++pt == min(G, tiles - pg * G)) {
-          pt = 0;
-          if (++pkc == nk) {
-            pkc = 0;
-            ++pg;
-          }
-        }
-      };
-      for (int i = 0; i < t32::kPrefetch; ++i) prefetch_next();
       int j = 0, jb = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
@@ -208,7 +187,6 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
               tma_load_2d(dst, &tmap_s, kc * t32::kKChunk, y, &stg_full[s]);
               tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
             }
-            prefetch_next();
             ++j;
           }
         }

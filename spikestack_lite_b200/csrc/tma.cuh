@@ -20,15 +20,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
       : "memory");
 }
 
-// Prefetch one box of a 2-D tensor map into L2 (no shared memory, no
-// barrier); a later tma_load_2d of the same box then reads L2 instead of HBM.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
