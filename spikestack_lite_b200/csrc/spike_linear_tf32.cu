@@ -19,8 +19,10 @@
 // rows, weight chunks by 1-D bulk copy), warp 1 TMEM owner + MMA issuer,
 // warps 2-17 converters (8 rows each), warps 18-21 epilogue (+ bias, store Y).
 // Slot protocol: stg_full (TMA) -> chk (all converters screened; hi rewritten
-// if needed) -> MMA [-> lo_go -> converters write lo -> lo_full -> MMA] ->
-// stg_empty (converters done reading/writing + the MMAs that read the slot).
+// if needed) -> hi MMAs -> lo_go [-> the non-exact warps write lo -> lo_full
+// -> lo MMAs] -> stg_empty (converters done reading/writing + the MMAs that
+// read the slot).  Converter warps whose rows are exact never wait inside a
+// slot: they arrive on chk, lo_full and stg_empty and move on.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; issued copies
 // and MMAs are drained and TMEM is freed on every exit.
 #include "tma.cuh"
@@ -152,14 +154,38 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // programmatic dependent of the weight-image kernel (image + cleared scan state)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Programmatic dependent of the weight-image kernel (image + cleared scan
+  // state).  That kernel is a plain launch, so S was complete before it
+  // started: the producer requests the first slots of S before its wait, and
+  // the converters screen them before theirs (ahead of their first global
+  // write).
+  const bool late_dep = (warp == 0 && lane == 0) || (warp >= 2 && warp < 2 + CW);
+  if (!late_dep) asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_map(&tmap_s);
+      auto load_s = [&](int s, int64_t row0, int kc) {
+        // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
+        // (rows a box leaves out keep stale data; the converters and the epilogue ignore them)
+        const int nbox = (int)ceil_div(min64(t32::kRows, r_end - row0), t32::kBoxRows);
+        mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(2 * nbox * t32::kBoxBytes));
+        for (int b = 0; b < nbox; ++b) {
+          unsigned char* dst = stg + s * t32::kStgBytes + b * t32::kBoxBytes;
+          const int y = (int)row0 + b * t32::kBoxRows;
+          tma_load_2d(dst, &tmap_s, kc * t32::kKChunk, y, &stg_full[s]);
+          tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
+        }
+      };
+      int pre = 0;  // slots requested before the wait: the first NS (or all)
+      for (int g = 0; g < groups && pre < NS; ++g) {
+        const int tg = min(G, tiles - g * G);
+        for (int kc = 0; kc < nk && pre < NS; ++kc)
+          for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(g * G + t) * t32::kRows, kc);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       int j = 0, jb = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
@@ -172,26 +198,18 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
           bulk_g2s(bst + (size_t)sb * C::kBBytes, a.wimg + ((size_t)n_tile * nk + kc) * C::kBBytes, C::kBBytes,
                    &b_full[sb]);
           ++jb;
-          for (int t = 0; t < tg; ++t) {
+          for (int t = 0; t < tg; ++t, ++j) {
+            if (j < pre) continue;
             const int s = j % NS;
             if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
               break;
-            const int64_t row0 = r_begin + (int64_t)(g * G + t) * t32::kRows;
-            // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
-            // (rows a box leaves out keep stale data; the converters and the epilogue ignore them)
-            const int nbox = (int)ceil_div(min64(t32::kRows, r_end - row0), t32::kBoxRows);
-            mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(2 * nbox * t32::kBoxBytes));
-            for (int b = 0; b < nbox; ++b) {
-              unsigned char* dst = stg + s * t32::kStgBytes + b * t32::kBoxBytes;
-              const int y = (int)row0 + b * t32::kBoxRows;
-              tma_load_2d(dst, &tmap_s, kc * t32::kKChunk, y, &stg_full[s]);
-              tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
-            }
-            ++j;
+            load_s(s, r_begin + (int64_t)(g * G + t) * t32::kRows, kc);
           }
         }
       }
-      for (int i = (j > NS ? j - NS : 0); i < j; ++i)
+      // copies still in flight land before the CTA exits (early exits included)
+      const int issued = max(j, pre);
+      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
         mbar_wait(&stg_full[i % NS], (i / NS) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
       for (int i = (jb > NB ? jb - NB : 0); i < jb; ++i)
         mbar_wait(&b_full[i % NB], (i / NB) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
@@ -201,7 +219,6 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_tf32_f32(t32::kRows, NT);
       int j = 0, jb = 0;
-      uint32_t lo_par = 0u;  // bit s: phase parity of lo_go / lo_full of staging slot s (they move only on lo passes)
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
         const int tg = min(G, tiles - g * G);
@@ -230,11 +247,12 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
               umma_tf32_ss(d, da, dbh, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
               umma_tf32_ss(d, da, dbl, idesc, 1u);
             }
+            // lo_go and lo_full complete once per slot use, lo pass or not, so
+            // that the phase parity of a use is (j / NS) & 1 for every waiter
+            umma_commit(&lo_go[s]);
             if (lo_any) {
               // the slot's warps rewrite it with the remainders once the hi MMAs have read it
-              umma_commit(&lo_go[s]);
-              if (!(ok = mbar_wait(&lo_full[s], (lo_par >> s) & 1u, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-              lo_par ^= 1u << s;
+              if (!(ok = mbar_wait(&lo_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < t32::kKChunk / 8; ++kk) {
@@ -282,8 +300,7 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
     const int my_i = (lane >> 1) & (NL - 1);
     const uint32_t my_sel = (lane & 1) ? 0x7632u : 0x5410u;
     int j = 0, s = 0;
-    uint32_t ps = 0u;
-    uint32_t lo_par = 0u;  // bit s: phase parity of lo_go / lo_full of staging slot s
+    uint32_t ps = 0u;  // phase parity of the current use of slot s
     bool ok = true;
     for (int g = 0; g < groups && ok; ++g) {
       const int tg = min(G, tiles - g * G);
@@ -343,28 +360,41 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
           if (lane == 0) lo_flag[s * CW + cw] = warp_lo ? 1 : 0;
           __syncwarp();
           if (lane == 0) mbar_arrive(&chk[s]);
-          // every converter learns whether any warp of the slot needs the lo pass
-          if (!(ok = mbar_wait(&chk[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-          int lo_any = 0;
+          if (warp_lo) {
+            // Lo pass, run by the warps whose rows were not exact: once every
+            // warp has screened (chk) and the hi MMAs have read the slot
+            // (lo_go), each writes its remainders, and the first of them
+            // zeroes the rows of the exact warps, which have moved on.
+            if (!(ok = mbar_wait(&chk[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+            uint32_t lo_mask = 0u;
 #pragma unroll
-          for (int w = 0; w < CW; ++w) lo_any |= lo_flag[s * CW + w];
-          if (lo_any) {
-            // lo pass: every row is rewritten with its remainder (0 for exact rows)
-            if (!(ok = mbar_wait(&lo_go[s], (lo_par >> s) & 1u, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-            lo_par ^= 1u << s;
+            for (int w = 0; w < CW; ++w) lo_mask |= lo_flag[s * CW + w] ? (1u << w) : 0u;
+            if (!(ok = mbar_wait(&lo_go[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
 #pragma unroll
-            for (int i = 0; i < NL; ++i) {
-              const float4 q = warp_lo ? make_float4(lo_v[i][0], lo_v[i][1], lo_v[i][2], lo_v[i][3])
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-              *reinterpret_cast<float4*>(st + soff[i]) = q;
+            for (int i = 0; i < NL; ++i)
+              *reinterpret_cast<float4*>(st + soff[i]) = make_float4(lo_v[i][0], lo_v[i][1], lo_v[i][2], lo_v[i][3]);
+            if (cw == __ffs((int)lo_mask) - 1) {
+              for (int w = 0; w < CW; ++w) {
+                if ((lo_mask >> w) & 1u) continue;
+#pragma unroll
+                for (int i = 0; i < NL; ++i) {
+                  const uint32_t off = (uint32_t)((cl >> 3) * t32::kAtomBytes) +
+                                       sw128_chunk((uint32_t)(w * RPW + 2 * i + half), (uint32_t)(cl & 7));
+                  *reinterpret_cast<float4*>(st + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+              }
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&lo_full[s]);
           }
-          // the slot's data is consumed (the ballots used every loaded value)
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&stg_empty[s]);
+          // lo_full completes on every slot use (the MMA waits for it only on
+          // a lo pass); the slot's data is consumed (the ballots used every
+          // loaded value)
+          if (lane == 0) {
+            mbar_arrive(&lo_full[s]);
+            mbar_arrive(&stg_empty[s]);
+          }
+          if (j == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
           if (emit) {
             uint32_t q[4];
 #pragma unroll

@@ -73,6 +73,28 @@ def test_real_valued_negative_and_nan_inputs(branch):
     assert O.rel_err(Y.cpu().numpy(), ref) < TOL
 
 
+@pytest.mark.parametrize("stride", [37, 300])
+def test_mixed_exact_and_real_rows(stride):
+    # spike rows with a few real-valued rows: within one 128-row tile some
+    # 8-row groups need the remainder pass and the others are exact, so the
+    # remainder pass has to clear the exact groups' rows
+    T, M, K = 2, 1500, 512
+    S = _spikes(T, M, K, 0.1, seed=stride)
+    g = torch.Generator(device="cuda").manual_seed(stride + 1)
+    rows = torch.arange(5, M, stride, device="cuda")
+    S[:, rows] = torch.randn(T, rows.numel(), K, generator=g, device="cuda") * 0.7
+    W = _weight(128, K, seed=stride + 2)
+    csr = ops.alloc_csr(T, M, K, "cuda", values=True)
+    Y = ops.spike_linear(S, weight=W, csr=csr, branch="dense")
+    Sn = S.cpu().numpy()
+    assert O.rel_err(Y.cpu().numpy(), O.spike_linear(Sn, W.t().cpu().numpy())) < TOL
+    exp = O.csr_planes(Sn)
+    n = int(exp[4][-1])
+    np.testing.assert_array_equal(csr["row_ptr"].cpu().numpy(), exp[1].reshape(-1))
+    np.testing.assert_array_equal(csr["col_idx"][:n].cpu().numpy(), exp[2])
+    np.testing.assert_array_equal(csr["values"][:n].cpu().numpy(), exp[3])
+
+
 @pytest.mark.parametrize("branch", ["dense", "csr"])
 def test_bias_and_golden(golden, branch):
     z = golden("spike_linear")
