@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(at::kThreads, 1)
       if (lane == 0) mbar_arrive(&km_empty[ab]);
     }
   }
-  __syncthreads();
+  role_join();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(at::kThreads, 1)
       ++ti;
     }
   }
-  __syncthreads();
+  role_join();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

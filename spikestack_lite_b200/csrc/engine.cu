@@ -5,6 +5,7 @@
 #include "spmm_csr.cu"
 #include "spike_linear_tc.cu"
 #include "spike_linear_tf32.cu"
+#include "spike_linear_wt.cu"
 #include "spike_linear.cu"
 #include "attention.cu"
 #include "attention_tc.cu"

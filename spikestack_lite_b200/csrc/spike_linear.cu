@@ -110,8 +110,11 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
       // value check only when CSR values are requested (spikes of 1 need no gather)
       if (values) o.nonunit = reinterpret_cast<int*>(wsb + L.csr_state) + 1;  // ScanState::nonunit
     }
-    rc = tf32 ? launch_tf32(S, (int64_t)T * M, K, N, p, img, o, stream)
-              : launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
+    // fp32 W with 128-column N tiles: weights in tensor memory (deeper S
+    // ring); narrower N: the S-as-A tf32 kernel with an N tile of N
+    if (tf32 && p.NT == 128) rc = launch_wt(S, (int64_t)T * M, K, N, p, img, o, stream);
+    else if (tf32) rc = launch_tf32(S, (int64_t)T * M, K, N, p, img, o, stream);
+    else rc = launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
     if (rc) return rc;
     if (want_csr) {
       rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, o.blk_sum, o.sup_sum, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,

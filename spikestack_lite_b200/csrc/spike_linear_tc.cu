@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
-  __syncthreads();
+  role_join();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);

@@ -92,6 +92,180 @@ __host__ __device__ __forceinline__ uint32_t sw128_chunk(uint32_t r, uint32_t c)
   return r * 128u + (((c ^ (r & 7u)) & 7u) << 4);
 }
 
+// ---------------------------------------------------------------- converters
+// Converter warps of the tf32 dense kernels (both operand orders share the
+// staging layout: 128 rows x 64 fp32 per slot, two 128-byte-swizzled atom
+// columns).  Warp cw of CW = 16 screens rows [8cw, 8cw+8) of every slot,
+// rewrites them for the exact hi/lo pass when needed, and emits the planar
+// spike masks, row counts and block sums of the CSR pass.
+template <int NS, int G>
+__device__ __forceinline__ void tf32_converter(const int cw, const int lane, unsigned char* stg, uint64_t* stg_full,
+                                               uint64_t* chk, uint64_t* stg_empty, uint64_t* lo_go,
+                                               uint64_t* lo_full, int* lo_flag, int* row_count,
+                                               volatile int* abort_flag, const TcArgs& a, const int64_t r_begin,
+                                               const int64_t r_end, const int n_tile, const int nk,
+                                               const int groups, const int tiles) {
+  constexpr int CW = t32::kConvWarps;
+  // Warp cw screens rows [8cw, 8cw+8) of each slot; in load i a lane holds
+  // columns 4(lane & 15) .. +3 of row 8cw + 2i + (lane >> 4) (16-byte chunk
+  // lane & 7 of atom column (lane >> 3) & 1).  The masks keep the planar
+  // format of the CSR pass: per row and 64-column chunk P0 = M0 | M1 << 16,
+  // P1 = M2 | M3 << 16, bit m of plane Me = column 4m + e.
+  const int half = lane >> 4;
+  const int cl = lane & 15;
+  const bool emit = (a.bitmap != nullptr) && n_tile == 0;
+  const bool check_unit = emit && a.nonunit != nullptr;
+  constexpr int RPW = t32::kRows / CW;  // rows per converter warp
+  constexpr int NL = RPW / 2;           // 16-byte loads per lane and slot
+  uint32_t soff[NL];
+  int rls[NL];
+#pragma unroll
+  for (int i = 0; i < NL; ++i) {
+    rls[i] = cw * RPW + 2 * i + half;
+    soff[i] = (uint32_t)((cl >> 3) * t32::kAtomBytes) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
+  }
+  const int my_i = (lane >> 1) & (NL - 1);
+  const uint32_t my_sel = (lane & 1) ? 0x7632u : 0x5410u;
+  int j = 0, s = 0;
+  uint32_t ps = 0u;  // phase parity of the current use of slot s
+  bool ok = true;
+  for (int g = 0; g < groups && ok; ++g) {
+    const int tg = min(G, tiles - g * G);
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      for (int t = 0; t < tg; ++t) {
+        if (!(ok = mbar_wait(&stg_full[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        const int64_t row0 = r_begin + (int64_t)(g * G + t) * t32::kRows;
+        const int nrows = (int)min64(t32::kRows, r_end - row0);
+        unsigned char* st = stg + s * t32::kStgBytes;
+        uint4 v[NL];  // raw fp32 bits; rows past nrows count as zero
+#pragma unroll
+        for (int i = 0; i < NL; ++i) {
+          v[i] = *reinterpret_cast<const uint4*>(st + soff[i]);
+          if (rls[i] >= nrows) v[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        // Screen: a sign bit, low 13 mantissa bits or an all-ones exponent
+        // (Inf/NaN; the OR of two other exponents can also give it, which
+        // only costs speed) anywhere in the warp's rows -> exact path.
+        uint32_t bits_or = 0u;
+        bool nonunit = false;
+        uint32_t m[NL][4];
+#pragma unroll
+        for (int i = 0; i < NL; ++i) {
+          const uint4 b = v[i];
+          bits_or |= b.x | b.y | b.z | b.w;
+          if (check_unit) {
+            nonunit |= (b.x != 0u && b.x != 0x3f800000u) || (b.y != 0u && b.y != 0x3f800000u) ||
+                       (b.z != 0u && b.z != 0x3f800000u) || (b.w != 0u && b.w != 0x3f800000u);
+          }
+          if (emit) {
+            m[i][0] = __ballot_sync(0xffffffffu, __uint_as_float(b.x) > 0.0f);
+            m[i][1] = __ballot_sync(0xffffffffu, __uint_as_float(b.y) > 0.0f);
+            m[i][2] = __ballot_sync(0xffffffffu, __uint_as_float(b.z) > 0.0f);
+            m[i][3] = __ballot_sync(0xffffffffu, __uint_as_float(b.w) > 0.0f);
+          }
+        }
+        const bool warp_lo =
+            __any_sync(0xffffffffu, (bits_or & 0x80001fffu) != 0u || (bits_or & 0x7f800000u) == 0x7f800000u);
+        float lo_v[NL][4];
+        if (warp_lo) {
+          // hi pass in place: relu'(x) rounded to tf32; the remainders wait in registers
+#pragma unroll
+          for (int i = 0; i < NL; ++i) {
+            const float x[4] = {__uint_as_float(v[i].x), __uint_as_float(v[i].y), __uint_as_float(v[i].z),
+                                __uint_as_float(v[i].w)};
+            float h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float xr = x[e] > 0.0f ? x[e] : 0.0f;
+              h[e] = tf32_rna(xr);
+              lo_v[i][e] = isfinite(xr) ? tf32_rna(xr - h[e]) : 0.0f;
+            }
+            *reinterpret_cast<float4*>(st + soff[i]) = make_float4(h[0], h[1], h[2], h[3]);
+          }
+          fence_proxy_async_smem();
+        }
+        if (lane == 0) lo_flag[s * CW + cw] = warp_lo ? 1 : 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&chk[s]);
+        if (warp_lo) {
+          // Lo pass, run by the warps whose rows were not exact: once every
+          // warp has screened (chk) and the hi MMAs have read the slot
+          // (lo_go), each writes its remainders, and the first of them
+          // zeroes the rows of the exact warps, which have moved on.
+          if (!(ok = mbar_wait(&chk[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          uint32_t lo_mask = 0u;
+#pragma unroll
+          for (int w = 0; w < CW; ++w) lo_mask |= lo_flag[s * CW + w] ? (1u << w) : 0u;
+          if (!(ok = mbar_wait(&lo_go[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+#pragma unroll
+          for (int i = 0; i < NL; ++i)
+            *reinterpret_cast<float4*>(st + soff[i]) = make_float4(lo_v[i][0], lo_v[i][1], lo_v[i][2], lo_v[i][3]);
+          if (cw == __ffs((int)lo_mask) - 1) {
+            for (int w = 0; w < CW; ++w) {
+              if ((lo_mask >> w) & 1u) continue;
+#pragma unroll
+              for (int i = 0; i < NL; ++i) {
+                const uint32_t off = (uint32_t)((cl >> 3) * t32::kAtomBytes) +
+                                     sw128_chunk((uint32_t)(w * RPW + 2 * i + half), (uint32_t)(cl & 7));
+                *reinterpret_cast<float4*>(st + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        // lo_full completes on every slot use (the MMA waits for it only on
+        // a lo pass); the slot's data is consumed (the ballots used every
+        // loaded value)
+        if (lane == 0) {
+          mbar_arrive(&lo_full[s]);
+          mbar_arrive(&stg_empty[s]);
+        }
+        if (j == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (emit) {
+          uint32_t q[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t x = m[0][e];
+#pragma unroll
+            for (int i = 1; i < NL; ++i) x = (my_i == i) ? m[i][e] : x;
+            q[e] = x;
+          }
+          const uint32_t keep0 = __byte_perm(q[0], q[1], my_sel);
+          const uint32_t keep1 = __byte_perm(q[2], q[3], my_sel);
+          const int rl = cw * RPW + lane;
+          if (lane < RPW && rl < nrows) {
+            const int64_t grow = row0 + rl;
+            const int idx = t * t32::kRows + rl;
+            const int c = __popc(keep0) + __popc(keep1);
+            const int total = (kc == 0 ? 0 : row_count[idx]) + c;
+            row_count[idx] = total;
+            *reinterpret_cast<uint2*>(a.bitmap + grow * a.KWP + 2 * kc) = make_uint2(keep0, keep1);
+            if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = total;
+          }
+          if (kc == nk - 1 && a.blk_sum) {
+            // the warp's 8 rows lie in one 128-row block: one atomic per warp and level
+            int cnt = (lane < RPW && rl < nrows) ? row_count[t * t32::kRows + rl] : 0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+            const int64_t g0 = row0 + cw * RPW;
+            if (lane == 0 && cw * RPW < nrows && cnt) {
+              atomicAdd(&a.blk_sum[g0 >> 7], cnt);
+              atomicAdd(&a.sup_sum[g0 >> 14], (unsigned long long)cnt);
+            }
+          }
+        }
+        if (check_unit && __any_sync(0xffffffffu, nonunit) && lane == 0) atomicOr(a.nonunit, 1);
+        ++j;
+        if (++s == NS) {
+          s = 0;
+          ps ^= 1u;
+        }
+      }
+    }
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(t32::kThreads, 1)
     spike_linear_tf32_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
@@ -277,166 +451,8 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
       }
     }
   } else if (warp < 2 + CW) {
-    // ---------------------------------------------------------------- converters
-    // Warp cw screens rows [8cw, 8cw+8) of each slot; in load i a lane holds
-    // columns 4(lane & 15) .. +3 of row 8cw + 2i + (lane >> 4) (16-byte chunk
-    // lane & 7 of atom column (lane >> 3) & 1).  The masks keep the planar
-    // format of the CSR pass: per row and 64-column chunk P0 = M0 | M1 << 16,
-    // P1 = M2 | M3 << 16, bit m of plane Me = column 4m + e.
-    const int cw = warp - 2;
-    const int half = lane >> 4;
-    const int cl = lane & 15;
-    const bool emit = (a.bitmap != nullptr) && n_tile == 0;
-    const bool check_unit = emit && a.nonunit != nullptr;
-    constexpr int RPW = t32::kRows / CW;  // rows per converter warp
-    constexpr int NL = RPW / 2;           // 16-byte loads per lane and slot
-    uint32_t soff[NL];
-    int rls[NL];
-#pragma unroll
-    for (int i = 0; i < NL; ++i) {
-      rls[i] = cw * RPW + 2 * i + half;
-      soff[i] = (uint32_t)((cl >> 3) * t32::kAtomBytes) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
-    }
-    const int my_i = (lane >> 1) & (NL - 1);
-    const uint32_t my_sel = (lane & 1) ? 0x7632u : 0x5410u;
-    int j = 0, s = 0;
-    uint32_t ps = 0u;  // phase parity of the current use of slot s
-    bool ok = true;
-    for (int g = 0; g < groups && ok; ++g) {
-      const int tg = min(G, tiles - g * G);
-      for (int kc = 0; kc < nk && ok; ++kc) {
-        for (int t = 0; t < tg; ++t) {
-          if (!(ok = mbar_wait(&stg_full[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-          const int64_t row0 = r_begin + (int64_t)(g * G + t) * t32::kRows;
-          const int nrows = (int)min64(t32::kRows, r_end - row0);
-          unsigned char* st = stg + s * t32::kStgBytes;
-          uint4 v[NL];  // raw fp32 bits; rows past nrows count as zero
-#pragma unroll
-          for (int i = 0; i < NL; ++i) {
-            v[i] = *reinterpret_cast<const uint4*>(st + soff[i]);
-            if (rls[i] >= nrows) v[i] = make_uint4(0u, 0u, 0u, 0u);
-          }
-          // Screen: a sign bit, low 13 mantissa bits or an all-ones exponent
-          // (Inf/NaN; the OR of two other exponents can also give it, which
-          // only costs speed) anywhere in the warp's rows -> exact path.
-          uint32_t bits_or = 0u;
-          bool nonunit = false;
-          uint32_t m[NL][4];
-#pragma unroll
-          for (int i = 0; i < NL; ++i) {
-            const uint4 b = v[i];
-            bits_or |= b.x | b.y | b.z | b.w;
-            if (check_unit) {
-              nonunit |= (b.x != 0u && b.x != 0x3f800000u) || (b.y != 0u && b.y != 0x3f800000u) ||
-                         (b.z != 0u && b.z != 0x3f800000u) || (b.w != 0u && b.w != 0x3f800000u);
-            }
-            if (emit) {
-              m[i][0] = __ballot_sync(0xffffffffu, __uint_as_float(b.x) > 0.0f);
-              m[i][1] = __ballot_sync(0xffffffffu, __uint_as_float(b.y) > 0.0f);
-              m[i][2] = __ballot_sync(0xffffffffu, __uint_as_float(b.z) > 0.0f);
-              m[i][3] = __ballot_sync(0xffffffffu, __uint_as_float(b.w) > 0.0f);
-            }
-          }
-          const bool warp_lo =
-              __any_sync(0xffffffffu, (bits_or & 0x80001fffu) != 0u || (bits_or & 0x7f800000u) == 0x7f800000u);
-          float lo_v[NL][4];
-          if (warp_lo) {
-            // hi pass in place: relu'(x) rounded to tf32; the remainders wait in registers
-#pragma unroll
-            for (int i = 0; i < NL; ++i) {
-              const float x[4] = {__uint_as_float(v[i].x), __uint_as_float(v[i].y), __uint_as_float(v[i].z),
-                                  __uint_as_float(v[i].w)};
-              float h[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float xr = x[e] > 0.0f ? x[e] : 0.0f;
-                h[e] = tf32_rna(xr);
-                lo_v[i][e] = isfinite(xr) ? tf32_rna(xr - h[e]) : 0.0f;
-              }
-              *reinterpret_cast<float4*>(st + soff[i]) = make_float4(h[0], h[1], h[2], h[3]);
-            }
-            fence_proxy_async_smem();
-          }
-          if (lane == 0) lo_flag[s * CW + cw] = warp_lo ? 1 : 0;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&chk[s]);
-          if (warp_lo) {
-            // Lo pass, run by the warps whose rows were not exact: once every
-            // warp has screened (chk) and the hi MMAs have read the slot
-            // (lo_go), each writes its remainders, and the first of them
-            // zeroes the rows of the exact warps, which have moved on.
-            if (!(ok = mbar_wait(&chk[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-            uint32_t lo_mask = 0u;
-#pragma unroll
-            for (int w = 0; w < CW; ++w) lo_mask |= lo_flag[s * CW + w] ? (1u << w) : 0u;
-            if (!(ok = mbar_wait(&lo_go[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-#pragma unroll
-            for (int i = 0; i < NL; ++i)
-              *reinterpret_cast<float4*>(st + soff[i]) = make_float4(lo_v[i][0], lo_v[i][1], lo_v[i][2], lo_v[i][3]);
-            if (cw == __ffs((int)lo_mask) - 1) {
-              for (int w = 0; w < CW; ++w) {
-                if ((lo_mask >> w) & 1u) continue;
-#pragma unroll
-                for (int i = 0; i < NL; ++i) {
-                  const uint32_t off = (uint32_t)((cl >> 3) * t32::kAtomBytes) +
-                                       sw128_chunk((uint32_t)(w * RPW + 2 * i + half), (uint32_t)(cl & 7));
-                  *reinterpret_cast<float4*>(st + off) = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-              }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-          }
-          // lo_full completes on every slot use (the MMA waits for it only on
-          // a lo pass); the slot's data is consumed (the ballots used every
-          // loaded value)
-          if (lane == 0) {
-            mbar_arrive(&lo_full[s]);
-            mbar_arrive(&stg_empty[s]);
-          }
-          if (j == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
-          if (emit) {
-            uint32_t q[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              uint32_t x = m[0][e];
-#pragma unroll
-              for (int i = 1; i < NL; ++i) x = (my_i == i) ? m[i][e] : x;
-              q[e] = x;
-            }
-            const uint32_t keep0 = __byte_perm(q[0], q[1], my_sel);
-            const uint32_t keep1 = __byte_perm(q[2], q[3], my_sel);
-            const int rl = cw * RPW + lane;
-            if (lane < RPW && rl < nrows) {
-              const int64_t grow = row0 + rl;
-              const int idx = t * t32::kRows + rl;
-              const int c = __popc(keep0) + __popc(keep1);
-              const int total = (kc == 0 ? 0 : row_count[idx]) + c;
-              row_count[idx] = total;
-              *reinterpret_cast<uint2*>(a.bitmap + grow * a.KWP + 2 * kc) = make_uint2(keep0, keep1);
-              if (kc == nk - 1 && a.row_cnt) a.row_cnt[grow] = total;
-            }
-            if (kc == nk - 1 && a.blk_sum) {
-              // the warp's 8 rows lie in one 128-row block: one atomic per warp and level
-              int cnt = (lane < RPW && rl < nrows) ? row_count[t * t32::kRows + rl] : 0;
-#pragma unroll
-              for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-              const int64_t g0 = row0 + cw * RPW;
-              if (lane == 0 && cw * RPW < nrows && cnt) {
-                atomicAdd(&a.blk_sum[g0 >> 7], cnt);
-                atomicAdd(&a.sup_sum[g0 >> 14], (unsigned long long)cnt);
-              }
-            }
-          }
-          if (check_unit && __any_sync(0xffffffffu, nonunit) && lane == 0) atomicOr(a.nonunit, 1);
-          ++j;
-          if (++s == NS) {
-            s = 0;
-            ps ^= 1u;
-          }
-        }
-      }
-    }
+    tf32_converter<NS, G>(warp - 2, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count, abort_flag,
+                          a, r_begin, r_end, n_tile, nk, groups, tiles);
   } else {
     // ---------------------------------------------------------------- epilogue (warps 18-21)
     // 16-lane x 256-bit TMEM loads: four threads per row, so every store
@@ -493,7 +509,7 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
-  __syncthreads();
+  role_join();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);

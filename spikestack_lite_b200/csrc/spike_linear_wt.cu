@@ -1,0 +1,392 @@
+// Dense branch of spike-linear for fp32 weights and N > 64: the weights live
+// in tensor memory as the A operand and the spikes stream through shared
+// memory as the B operand (tcgen05.mma kind::tf32, A from TMEM).
+//
+// Per 128-column N tile the kernel computes Y^T[n, r] = sum_k W^T[n, k] *
+// relu'(S[r, k]) (+ bias[n]) with relu'(x) = x if x > 0 else 0 (the reference
+// engine's predicate, sparse_linear.cu:268): MMA M = the 128 output columns
+// (TMEM lanes), MMA N = 128 rows of S, K = 64 per staging slot.  W is split
+// into tf32 hi + lo halves (W = hi + lo to ~2^-22 relative), two MMAs per
+// k-step; S arrives fp32 straight from TMA into the staging slot, which is
+// the K-major B operand as it lies.  Non-exact S values (low mantissa bits,
+// negative, Inf/NaN) take the same hi pass / lo pass in place as in the
+// S-as-A kernel (spike_linear_tf32.cu), with the converter warps shared.
+//
+// Why this operand order: the S-as-A kernel keeps two 64 KB weight chunks in
+// shared memory for the whole time the MMAs read them, leaving room for three
+// 32 KB S slots, too few to cover the DRAM latency of a slot.  Here a weight
+// chunk passes through shared memory only briefly (16 KB pieces, copied into
+// TMEM by four warps), so five S slots fit.
+//
+// TMEM (512 columns): [0, 256) two weight chunks, each [hi k0..63 | lo k0..63]
+// (one tf32 per column, lane = output column n); [256, 512) the accumulators
+// of a group of two row tiles (column = row, lane = n), single-buffered.
+//
+// Warp roles (736 threads): warp 0 S producer (TMA, boxes of 32 columns x 32
+// rows), warp 1 TMEM owner + MMA issuer, warp 2 weight-piece producer (1-D
+// bulk copies), warps 3-18 converters, warps 19-22 weight loaders (shared
+// memory piece -> tcgen05.st into TMEM) and epilogue (TMEM -> + bias -> Y).
+// Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; issued copies
+// and MMAs are drained and TMEM is freed on every exit.
+#include "tma.cuh"
+
+namespace spk {
+
+namespace wt {
+
+constexpr int kRows = 128;                  // rows of S per tile (MMA N)
+constexpr int kLanes = 128;                 // output columns per tile (MMA M, TMEM lanes)
+constexpr int kKChunk = 64;                 // columns of S per staging slot
+constexpr int kAtomBytes = kRows * 128;     // one swizzle-atom column of a slot: 16 KB
+constexpr int kStgBytes = 2 * kAtomBytes;   // 32 KB
+constexpr int kBoxRows = 32;
+constexpr int kBoxBytes = kBoxRows * 128;
+constexpr int kPieceBytes = kLanes * 128;   // 128 n x 32 k of hi or lo: 16 KB
+constexpr int kPieces = 4;                  // per 64-wide K chunk: hi k0-31, hi k32-63, lo k0-31, lo k32-63
+constexpr int kConvWarps = t32::kConvWarps;
+constexpr int kNS = 5;                      // staging slots
+constexpr int kNP = 4;                      // weight-piece slots
+constexpr int kG = 2;                       // row tiles per accumulator group
+constexpr int kWarps = 3 + kConvWarps + 4;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 columns
+constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
+constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNP * kPieceBytes;
+// barriers (5 NS + 2 NP + 7), lo flags [NS][16], row counts [G][128], TMEM slot, abort flag
+constexpr size_t kTail = 8 * (5 * kNS + 2 * kNP + 7) + 4 * kConvWarps * kNS + 4 * kRows * kG + 16;
+constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kDcol + kG * kRows <= kTmemCols && kAcol + 2 * 2 * kKChunk <= kDcol, "TMEM budget");
+static_assert(kRows == t32::kRows && kStgBytes == t32::kStgBytes, "staging layout shared with the converters");
+
+}  // namespace wt
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(wt::kThreads, 1)
+    spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
+  constexpr int G = wt::kG, NS = wt::kNS, NP = wt::kNP, CW = wt::kConvWarps;
+  extern __shared__ __align__(1024) unsigned char smem_dyn[];
+  unsigned char* base = smem_aligned_1024(smem_dyn);
+  unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
+  unsigned char* pcs = stg + NS * wt::kStgBytes;              // [NP][16 KB] weight pieces
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes);
+  uint64_t* stg_full = bars;
+  uint64_t* chk = stg_full + NS;
+  uint64_t* stg_empty = chk + NS;
+  uint64_t* lo_go = stg_empty + NS;
+  uint64_t* lo_full = lo_go + NS;
+  uint64_t* pc_full = lo_full + NS;
+  uint64_t* pc_empty = pc_full + NP;
+  uint64_t* a_full = pc_empty + NP;   // [2] weight chunk in TMEM
+  uint64_t* a_empty = a_full + 2;     // [2]
+  uint64_t* acc_full = a_empty + 2;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_empty + 1;
+  int* lo_flag = reinterpret_cast<int*>(drain + 1);               // [NS][CW]
+  int* row_count = lo_flag + NS * CW;                               // [G][128]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r_begin = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t r_end = min64(a.R, r_begin + a.rows_per_cta);
+  const int n_tile = blockIdx.y;
+  const int n0 = n_tile * wt::kLanes;
+  const int nk = a.nk;
+  const int tiles = r_end > r_begin ? (int)ceil_div(r_end - r_begin, wt::kRows) : 0;
+  const int groups = (tiles + G - 1) / G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&stg_full[s], 1);
+      mbar_init(&chk[s], CW);
+      mbar_init(&stg_empty[s], CW + 1);
+      mbar_init(&lo_go[s], 1);
+      mbar_init(&lo_full[s], CW);
+    }
+    for (int p = 0; p < NP; ++p) {
+      mbar_init(&pc_full[p], 1);
+      mbar_init(&pc_empty[p], 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&a_full[b], 4);
+      mbar_init(&a_empty[b], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, wt::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent of the weight-image kernel (image + cleared scan
+  // state).  That kernel is a plain launch, so S was complete before it
+  // started: the S producer requests the first slots before its wait, and the
+  // converters screen them before theirs (ahead of their first global write).
+  const bool late_dep = (warp == 0 && lane == 0) || (warp >= 3 && warp < 3 + CW);
+  if (!late_dep) asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- S producer
+    if (lane == 0) {
+      tma_prefetch_map(&tmap_s);
+      auto load_s = [&](int s, int64_t row0, int kc) {
+        // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
+        // (rows a box leaves out keep stale data; the converters and the epilogue ignore them)
+        const int nbox = (int)ceil_div(min64(wt::kRows, r_end - row0), wt::kBoxRows);
+        mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(2 * nbox * wt::kBoxBytes));
+        for (int b = 0; b < nbox; ++b) {
+          unsigned char* dst = stg + s * wt::kStgBytes + b * wt::kBoxBytes;
+          const int y = (int)row0 + b * wt::kBoxRows;
+          tma_load_2d(dst, &tmap_s, kc * wt::kKChunk, y, &stg_full[s]);
+          tma_load_2d(dst + wt::kAtomBytes, &tmap_s, kc * wt::kKChunk + 32, y, &stg_full[s]);
+        }
+      };
+      int pre = 0;  // slots requested before the wait: the first NS (or all)
+      for (int g = 0; g < groups && pre < NS; ++g) {
+        const int tg = min(G, tiles - g * G);
+        for (int kc = 0; kc < nk && pre < NS; ++kc)
+          for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(g * G + t) * wt::kRows, kc);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      int j = 0;
+      bool ok = true;
+      for (int g = 0; g < groups && ok; ++g) {
+        const int tg = min(G, tiles - g * G);
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          for (int t = 0; t < tg; ++t, ++j) {
+            if (j < pre) continue;
+            const int s = j % NS;
+            if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
+              break;
+            load_s(s, r_begin + (int64_t)(g * G + t) * wt::kRows, kc);
+          }
+        }
+      }
+      // copies still in flight land before the CTA exits (early exits included)
+      const int issued = max(j, pre);
+      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+        mbar_wait(&stg_full[i % NS], (i / NS) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_tf32_f32(wt::kLanes, wt::kRows);
+      int j = 0, ja = 0;
+      bool ok = true;
+      for (int g = 0; g < groups && ok; ++g) {
+        const int tg = min(G, tiles - g * G);
+        // the accumulators are single-buffered: the previous group's epilogue has read them
+        if (g >= 1 && !(ok = mbar_wait(acc_empty, (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        tc_fence_after();
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          const int ab = ja & 1;
+          if (!(ok = mbar_wait(&a_full[ab], (ja >> 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          tc_fence_after();
+          const uint32_t a_hi = tmem + wt::kAcol + (uint32_t)ab * 128u;
+          const uint32_t a_lo = a_hi + 64u;
+          for (int t = 0; t < tg; ++t) {
+            const int s = j % NS;
+            if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+            tc_fence_after();
+            int lo_any = 0;
+#pragma unroll
+            for (int w = 0; w < CW; ++w) lo_any |= lo_flag[s * CW + w];
+            const uint32_t d = tmem + wt::kDcol + (uint32_t)(t * wt::kRows);
+            const uint32_t bsm = smem_u32(stg + s * wt::kStgBytes);
+#pragma unroll
+            for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
+              const uint32_t atom = (uint32_t)(kk >> 2), kof = (uint32_t)(kk & 3) * 32u;
+              const uint64_t db = umma_desc_sw128_kmajor(bsm + atom * wt::kAtomBytes + kof);
+              umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+              umma_tf32_ts(d, a_lo + (uint32_t)kk * 8u, db, idesc, 1u);
+            }
+            // lo_go and lo_full complete once per slot use, lo pass or not
+            umma_commit(&lo_go[s]);
+            if (lo_any) {
+              // the slot's warps rewrite it with the remainders once the hi MMAs have read it
+              if (!(ok = mbar_wait(&lo_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
+                const uint32_t atom = (uint32_t)(kk >> 2), kof = (uint32_t)(kk & 3) * 32u;
+                const uint64_t db = umma_desc_sw128_kmajor(bsm + atom * wt::kAtomBytes + kof);
+                umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db, idesc, 1u);
+              }
+            }
+            umma_commit(&stg_empty[s]);
+            ++j;
+          }
+          if (!ok) break;
+          umma_commit(&a_empty[ab]);
+          ++ja;
+        }
+        if (ok) umma_commit(acc_full);
+      }
+      if (!ok) {  // issued MMAs finish before TMEM and shared memory are released
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- weight-piece producer
+    if (lane == 0) {
+      int jp = 0;
+      bool ok = true;
+      const unsigned char* img = a.wimg + (size_t)n_tile * nk * wt::kPieces * wt::kPieceBytes;
+      for (int c = 0; c < groups * nk && ok; ++c) {
+        const int kc = c % nk;
+        for (int p = 0; p < wt::kPieces; ++p, ++jp) {
+          const int sp = jp % NP;
+          if (jp >= NP && !(ok = mbar_wait(&pc_empty[sp], ((jp / NP) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
+            break;
+          mbar_arrive_expect_tx(&pc_full[sp], wt::kPieceBytes);
+          bulk_g2s(pcs + (size_t)sp * wt::kPieceBytes, img + ((size_t)kc * wt::kPieces + p) * wt::kPieceBytes,
+                   wt::kPieceBytes, &pc_full[sp]);
+        }
+      }
+      for (int i = (jp > NP ? jp - NP : 0); i < jp; ++i)
+        mbar_wait(&pc_full[i % NP], (i / NP) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
+    }
+  } else if (warp < 3 + CW) {
+    tf32_converter<NS, G>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count, abort_flag,
+                          a, r_begin, r_end, n_tile, nk, groups, tiles);
+  } else {
+    // ---------------------------------------------------------------- weight loaders + epilogue (warps 19-22)
+    // Warp q = warp & 3 owns TMEM lanes [32q, 32q+32): output columns n0 + 32q + lane.
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int nl = q * 32 + lane;
+    const int n = n0 + nl;
+    const float bias_n = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.0f;
+    const int total_chunks = groups * nk;
+    int ja = 0, jp = 0;
+    bool ok = true;
+    // one 64-wide K chunk of the weights: four 16 KB pieces -> TMEM buffer ja & 1
+    auto load_chunk = [&]() -> bool {
+      const int ab = ja & 1;
+      if (ja >= 2 && !mbar_wait(&a_empty[ab], ((ja >> 1) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
+      tc_fence_after();
+      for (int p = 0; p < wt::kPieces; ++p, ++jp) {
+        const int sp = jp % NP;
+        if (!mbar_wait(&pc_full[sp], (jp / NP) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
+        const unsigned char* src = pcs + (size_t)sp * wt::kPieceBytes;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + sw128_chunk((uint32_t)nl, (uint32_t)c));
+          r[4 * c] = v.x;
+          r[4 * c + 1] = v.y;
+          r[4 * c + 2] = v.z;
+          r[4 * c + 3] = v.w;
+        }
+        tmem_st_32x32b_x32(tmem + lane_base + wt::kAcol + (uint32_t)(ab * 128 + p * 32), r);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pc_empty[sp]);  // the piece's words are in registers / issued
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[ab]);
+      ++ja;
+      return true;
+    };
+    for (int g = 0; g < groups && ok; ++g) {
+      const int tg = min(G, tiles - g * G);
+      // this group's chunks, then the next group's first two (their buffers
+      // free up with this group's last MMAs), then this group's epilogue
+      while (ok && ja < min(total_chunks, (g + 1) * nk + 2)) ok = load_chunk();
+      if (!ok) break;
+      if (!(ok = mbar_wait(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+      tc_fence_after();
+      for (int t = 0; t < tg; ++t) {
+        const int64_t row0 = r_begin + (int64_t)(g * G + t) * wt::kRows;
+#pragma unroll 1
+        for (int rb = 0; rb < wt::kRows; rb += 16) {
+          if (row0 + rb >= r_end) break;
+          float v[16];
+          tmem_ld16(tmem + lane_base + wt::kDcol + (uint32_t)(t * wt::kRows + rb), v);
+          tmem_wait_ld();
+          tmem_reg_fence(v);
+          if (n < a.N) {
+            float* y = a.Y + (row0 + rb) * a.N + n;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              if (row0 + rb + jj < r_end) y[(int64_t)jj * a.N] = v[jj] + bias_n;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+    tmem_wait_st();
+  }
+
+  role_join();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, wt::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+// The weight image is the tf32 kernel's (tf32_img_bytes, w_image_tf32_kernel)
+// with NT = 128: per N tile and K chunk the pieces hi k0-31 | hi k32-63 |
+// lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle.
+int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
+              cudaStream_t stream) {
+  if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
+  CUtensorMap map;
+  int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
+  if (rc) return rc;
+  TcArgs a{};
+  a.R = R;
+  a.K = K;
+  a.N = N;
+  a.nk = p.nk;
+  a.KWP = 2 * p.nk;
+  a.wimg = img;
+  a.bias = o.bias;
+  a.Y = o.Y;
+  a.y_vec = 0;
+  a.bitmap = o.bitmap;
+  a.row_cnt = o.row_cnt;
+  a.nonunit = o.nonunit;
+  a.blk_sum = o.blk_sum;
+  a.sup_sum = o.sup_sum;
+  SPK_CUDA_TRY(cudaFuncSetAttribute(spike_linear_wt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)wt::kSmemBytes));
+  const int sms = sm_count();
+  const int ranges = sms / p.n_tiles > 0 ? sms / p.n_tiles : 1;
+  a.rows_per_cta = ceil_div(ceil_div(a.R, ranges), 32) * 32;
+  const int64_t gx = ceil_div(a.R, a.rows_per_cta);
+  dim3 grid((unsigned)gx, (unsigned)p.n_tiles);
+  prof_before(SPK_KERNEL_DENSE, stream);
+  SPK_CUDA_TRY(launch_dependent(spike_linear_wt_kernel, grid, dim3(wt::kThreads), wt::kSmemBytes, stream, map, a));
+  prof_after(SPK_KERNEL_DENSE, stream);
+  SPK_LAUNCH_CHECK();
+  count_launch(1);
+  return SPK_OK;
+}
+
+}  // namespace spk
