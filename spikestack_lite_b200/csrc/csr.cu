@@ -346,17 +346,22 @@ __device__ __forceinline__ void prefix_from_sums(const CsrArgs& a, int64_t r0, i
 // into a per-warp shared buffer and the warp copies it out with coalesced
 // stores (a warp whose rows hold more than kWarpBuf spikes, or whose values
 // are requested, writes straight to global memory).
-// Two lanes per row, each taking half of the row's 64-column chunks: the lanes
-// are ordered (row, half), so one warp-wide scan of the half counts gives every
-// half its first slot, and each lane's serial expansion is half a row long.
-// A warp's 16 rows are contiguous in col_idx: lanes expand into a per-warp
-// shared buffer and the warp copies it out with coalesced stores (a warp whose
-// rows hold more than kWarpBuf spikes, or whose values are requested, writes
-// straight to global memory).
-constexpr int kMaskRows = 128;                 // rows per CTA
-constexpr int kMaskThreads = 2 * kMaskRows;     // two lanes per row, each half of the row's chunks
+// Four lanes per row, each taking a quarter of the row's 64-column chunks:
+// the lanes are ordered (row, quarter), so one warp-wide scan of the quarter
+// counts gives every quarter its first slot, each lane's serial expansion is
+// a quarter row long, and twice as many warps are in flight as with two lanes
+// per row (the pass is latency-bound).
+// A warp's 8 rows are contiguous in col_idx: lanes expand into a per-warp
+// shared buffer, placed at the same offset modulo 16 bytes as the warp's
+// segment of col_idx, and the warp copies it out with 16-byte stores (a warp
+// whose rows hold more than kWarpBuf - 3 spikes, or whose values are
+// requested, writes straight to global memory).
+constexpr int kLanesPerRow = 4;
+constexpr int kMaskRows = 64;                              // rows per CTA
+constexpr int kMaskThreads = kLanesPerRow * kMaskRows;
 constexpr int kMaskWarps = kMaskThreads / 32;
-constexpr int kWarpBuf = 1024;                  // column slots staged per warp (16 rows)
+constexpr int kRowsPerWarp = 32 / kLanesPerRow;
+constexpr int kWarpBuf = 1024;                              // column slots staged per warp
 constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
 
 __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
@@ -369,16 +374,17 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   const int plane = (int)(blockIdx.x / tiles_pp);
   const int64_t row0 = (blockIdx.x % tiles_pp) * kMaskRows;  // row within the plane
   const int64_t grow0 = (int64_t)plane * a.M + row0;
-  const int rl = warp * 16 + (lane >> 1), hf = lane & 1;  // row in the CTA, half of its chunks
+  const int rl = warp * kRowsPerWarp + lane / kLanesPerRow;  // row in the CTA
+  const int qr = lane % kLanesPerRow;                          // quarter of its chunks
   const int64_t r = row0 + rl;
   const bool valid = r < a.M;
   const int64_t grow = grow0 + rl;
-  const int nch = a.KWP / 2, nh0 = (nch + 1) / 2;
-  const int c0 = hf ? nh0 : 0, c1 = hf ? nch : nh0;
+  const int nch = a.KWP / 2, per = (nch + kLanesPerRow - 1) / kLanesPerRow;
+  const int c0 = min(nch, qr * per), c1 = min(nch, c0 + per);
   const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow * a.KWP);
   constexpr int kPre = 4;  // mask chunks fetched ahead of the prefix computation
   uint2 pre_w[kPre];
-  int cnt = 0;            // spikes in this half of the row
+  int cnt = 0;            // spikes in this quarter of the row
 #pragma unroll
   for (int c = 0; c < kPre; ++c) {
     pre_w[c] = (valid && c0 + c < c1) ? __ldg(src + c0 + c) : make_uint2(0u, 0u);
@@ -406,8 +412,10 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   }
   const int64_t pos = pre_tile + wbase + incl - cnt;
   const int64_t rel = pre_tile - pre_plane;
-  const int cnt_row = cnt + __shfl_xor_sync(0xffffffffu, cnt, 1);  // both halves
-  if (valid && hf == 1) {
+  int cnt_row = cnt;  // all quarters of the row
+#pragma unroll
+  for (int o = 1; o < kLanesPerRow; o <<= 1) cnt_row += __shfl_xor_sync(0xffffffffu, cnt_row, o);
+  if (valid && qr == kLanesPerRow - 1) {
     a.row_ptr[(int64_t)plane * (a.M + 1) + r + 1] = (int32_t)(rel + wbase + incl);
     if (a.nnz_row) a.nnz_row[grow] = cnt_row;
   }
@@ -420,13 +428,15 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   }
   const int wtot = s_wtot[warp];
   const int64_t wstart = pre_tile + wbase;
-  const bool staged = a.values == nullptr && wtot <= kWarpBuf && wstart + wtot <= a.col_capacity;
+  // the warp's segment starts `sh` ints past a 16-byte boundary of col_idx
+  const int sh = (int)((reinterpret_cast<uintptr_t>(a.col_idx + wstart) >> 2) & 3u);
+  const bool staged = a.values == nullptr && wtot + 3 <= kWarpBuf && wstart + wtot <= a.col_capacity;
   int32_t* wbuf = s_buf_all + warp * kWarpBuf;
   if (cnt > 0) {
     const bool unit_values = a.state->nonunit == 0;
     const float* row = a.S + grow * a.K;
     const bool fits = staged || pos + cnt <= a.col_capacity;
-    int32_t* dst = staged ? wbuf + (incl - cnt) : a.col_idx + (fits ? pos : 0);
+    int32_t* dst = staged ? wbuf + sh + (incl - cnt) : a.col_idx + (fits ? pos : 0);
     float* vdst = a.values ? a.values + (fits ? pos : 0) : nullptr;
     int k = 0;
     bool overflow = false;
@@ -484,7 +494,15 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   if (staged) {
     __syncwarp();
     int32_t* g = a.col_idx + wstart;
-    for (int i = lane; i < wtot; i += 32) g[i] = wbuf[i];
+    // g[i] = wbuf[sh + i]: a head of up to 3 ints, 16-byte vectors, a tail
+    const int head = min(wtot, (4 - sh) & 3);
+    if (lane < head) g[lane] = wbuf[sh + lane];
+    const int nvec = (wtot - head) >> 2;
+    const int4* s4 = reinterpret_cast<const int4*>(wbuf + sh + head);
+    int4* g4 = reinterpret_cast<int4*>(g + head);
+    for (int q = lane; q < nvec; q += 32) g4[q] = s4[q];
+    const int done = head + 4 * nvec;
+    if (lane < wtot - done) g[done + lane] = wbuf[sh + done + lane];
   }
 }
 
