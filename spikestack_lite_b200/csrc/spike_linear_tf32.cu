@@ -51,8 +51,9 @@ struct Cfg {
   static constexpr int kBAtom = NT * 128;            // one swizzle-atom column of the weight chunk
   static constexpr int kBBytes = 4 * kBAtom;         // hi (2 atoms) + lo (2 atoms)
   static constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNB * kBBytes;
-  // barriers (5 NS + 2 NB + 5), lo flags [NS][16], row counts [G][128], TMEM slot, abort flag
-  static constexpr size_t kTail = 8 * (5 * kNS + 2 * kNB + 5) + 4 * kConvWarps * kNS + 4 * 128 * kG + 16;
+  // barriers (5 NS + 2 NB + 5), lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
+  static constexpr size_t kTail = 8 * (5 * kNS + 2 * kNB + 5) + kConvWarps * kNS + 4 * 128 * kG + 16;
+  static_assert((8 * (5 * kNS + 2 * kNB + 5)) % 16 == 0, "lo flags 16-byte aligned");
   static constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 128, "NT must be a multiple of 16 in [16, 128]");
   static_assert(kTmemCols <= 512, "TMEM budget");
@@ -101,7 +102,7 @@ __host__ __device__ __forceinline__ uint32_t sw128_chunk(uint32_t r, uint32_t c)
 template <int NS, int G>
 __device__ __forceinline__ void tf32_converter(const int cw, const int lane, unsigned char* stg, uint64_t* stg_full,
                                                uint64_t* chk, uint64_t* stg_empty, uint64_t* lo_go,
-                                               uint64_t* lo_full, int* lo_flag, int* row_count,
+                                               uint64_t* lo_full, uint8_t* lo_flag, int* row_count,
                                                volatile int* abort_flag, const TcArgs& a, const int64_t r_begin,
                                                const int64_t r_end, const int n_tile, const int nk,
                                                const int groups, const int tiles) {
@@ -184,7 +185,7 @@ __device__ __forceinline__ void tf32_converter(const int cw, const int lane, uns
           }
           fence_proxy_async_smem();
         }
-        if (lane == 0) lo_flag[s * CW + cw] = warp_lo ? 1 : 0;
+        if (lane == 0) lo_flag[s * CW + cw] = warp_lo ? 1u : 0u;
         __syncwarp();
         if (lane == 0) mbar_arrive(&chk[s]);
         if (warp_lo) {
@@ -286,8 +287,8 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
   uint64_t* acc_full = b_empty + NB;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  int* lo_flag = reinterpret_cast<int*>(drain + 1);              // [NS][CW]
-  int* row_count = lo_flag + NS * CW;                              // [G][128]
+  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(drain + 1);      // [NS][CW] bytes, 16-byte aligned
+  int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);      // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * t32::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -407,9 +408,8 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
             const int s = j % NS;
             if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
             tc_fence_after();
-            int lo_any = 0;
-#pragma unroll
-            for (int w = 0; w < CW; ++w) lo_any |= lo_flag[s * CW + w];
+            const uint4 lf = *reinterpret_cast<const uint4*>(lo_flag + s * CW);  // the 16 warps' flags
+            const bool lo_any = (lf.x | lf.y | lf.z | lf.w) != 0u;
             const uint32_t d = tmem + (uint32_t)(ab * C::kAccCols + t * C::kTileCols);
             const uint32_t asm_ = smem_u32(stg + s * t32::kStgBytes);
 #pragma unroll

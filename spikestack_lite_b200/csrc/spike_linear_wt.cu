@@ -53,8 +53,9 @@ constexpr int kTmemCols = 512;
 constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 columns
 constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
 constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNP * kPieceBytes;
-// barriers (5 NS + 2 NP + 7), lo flags [NS][16], row counts [G][128], TMEM slot, abort flag
-constexpr size_t kTail = 8 * (5 * kNS + 2 * kNP + 7) + 4 * kConvWarps * kNS + 4 * kRows * kG + 16;
+// barriers (5 NS + 2 NP + 7), lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
+constexpr size_t kTail = 8 * (5 * kNS + 2 * kNP + 7) + kConvWarps * kNS + 4 * kRows * kG + 16;
+static_assert((8 * (5 * kNS + 2 * kNP + 7)) % 16 == 0, "lo flags 16-byte aligned");
 constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kDcol + kG * kRows <= kTmemCols && kAcol + 2 * 2 * kKChunk <= kDcol, "TMEM budget");
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
-  int* lo_flag = reinterpret_cast<int*>(drain + 1);               // [NS][CW]
-  int* row_count = lo_flag + NS * CW;                               // [G][128]
+  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(drain + 1);       // [NS][CW] bytes, 16-byte aligned
+  int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -208,15 +209,15 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
             const int s = j % NS;
             if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
             tc_fence_after();
-            int lo_any = 0;
-#pragma unroll
-            for (int w = 0; w < CW; ++w) lo_any |= lo_flag[s * CW + w];
+            const uint4 lf = *reinterpret_cast<const uint4*>(lo_flag + s * CW);  // the 16 warps' flags
+            const bool lo_any = (lf.x | lf.y | lf.z | lf.w) != 0u;
             const uint32_t d = tmem + wt::kDcol + (uint32_t)(t * wt::kRows);
-            const uint32_t bsm = smem_u32(stg + s * wt::kStgBytes);
+            // k-step kk starts (kk >> 2) atoms + 32 (kk & 3) bytes into the slot: the descriptor's
+            // address field (bytes >> 4, no carry out for shared-memory addresses) advances by that
+            const uint64_t db0 = umma_desc_sw128_kmajor(smem_u32(stg + s * wt::kStgBytes));
 #pragma unroll
             for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
-              const uint32_t atom = (uint32_t)(kk >> 2), kof = (uint32_t)(kk & 3) * 32u;
-              const uint64_t db = umma_desc_sw128_kmajor(bsm + atom * wt::kAtomBytes + kof);
+              const uint64_t db = db0 + (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
               umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
               umma_tf32_ts(d, a_lo + (uint32_t)kk * 8u, db, idesc, 1u);
             }
@@ -228,8 +229,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
-                const uint32_t atom = (uint32_t)(kk >> 2), kof = (uint32_t)(kk & 3) * 32u;
-                const uint64_t db = umma_desc_sw128_kmajor(bsm + atom * wt::kAtomBytes + kof);
+                const uint64_t db = db0 + (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
                 umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db, idesc, 1u);
               }
             }
