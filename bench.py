@@ -248,7 +248,8 @@ def run_spike_linear(args, dist, cfg):
         "step_gbs": round(alg_step / (step_ms / 1e3) / 1e9, 1),
         "step_hbm_frac": round(alg_step / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
         "kernel_ms": {k: round(v, 5) for k, v in kernel_ms.items()},
-        "roofline": {"kernel": ("spike_linear_tf32_kernel" if cfg["w_dtype"] == "f32" else "spike_linear_tc_kernel")
+        "roofline": {"kernel": (("spike_linear_wt_kernel" if N > 64 else "spike_linear_tf32_kernel")
+                                if cfg["w_dtype"] == "f32" else "spike_linear_tc_kernel")
                      if dom == "dense" else "spmm_csr_kernel", **roof, "peak_src": pk["src"]},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "parity_rel_err": parity,
