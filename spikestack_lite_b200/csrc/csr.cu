@@ -382,7 +382,23 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   const int nch = a.KWP / 2, per = (nch + kLanesPerRow - 1) / kLanesPerRow;
   const int c0 = min(nch, qr * per), c1 = min(nch, c0 + per);
   const uint2* src = reinterpret_cast<const uint2*>(a.bitmap + grow * a.KWP);
-  constexpr int kPre = 4;  // mask chunks fetched ahead of the prefix computation
+  // All loads of the prologue go out together: this thread's share of the
+  // CTA's two prefix sums (spikes before the CTA's first row in the whole
+  // grid and before its plane: super-block, block and row counts) and the
+  // row's first mask chunks.
+  int64_t part[2] = {0, 0};
+  {
+    const int64_t at[2] = {grow0, (int64_t)plane * a.M};
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t rr = at[q];
+      const int64_t s_end = rr >> 14, b0 = s_end << 7, b1 = rr >> 7;
+      for (int64_t i = threadIdx.x; i < s_end; i += blockDim.x) part[q] += (int64_t)a.sup_sum[i];
+      for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) part[q] += a.blk_sum[i];
+      for (int64_t i = (b1 << 7) + threadIdx.x; i < rr; i += blockDim.x) part[q] += a.row_cnt[i];
+    }
+  }
+  constexpr int kPre = 4;  // mask chunks fetched ahead
   uint2 pre_w[kPre];
   int cnt = 0;            // spikes in this quarter of the row
 #pragma unroll
@@ -394,19 +410,31 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
     const uint2 pw = __ldg(src + c);
     cnt += __popc(pw.x) + __popc(pw.y);
   }
-  int64_t pre_tile, pre_plane;
-  prefix_from_sums(a, grow0, (int64_t)plane * a.M, s_red, pre_tile, pre_plane);
+  // warp-level: the prefix partials and the scan of the quarter counts, then
+  // one CTA barrier for both
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+    part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
+  }
   int incl = cnt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += y;
   }
-  if (lane == 31) s_wtot[warp] = incl;
+  if (lane == 31) {
+    s_wtot[warp] = incl;
+    s_red[warp] = part[0];
+    s_red[kMaskWarps + warp] = part[1];
+  }
   __syncthreads();
+  int64_t pre_tile = 0, pre_plane = 0;
   int wbase = 0, ctot = 0;
 #pragma unroll
   for (int w = 0; w < kMaskWarps; ++w) {
+    pre_tile += s_red[w];
+    pre_plane += s_red[kMaskWarps + w];
     wbase += (w < warp) ? s_wtot[w] : 0;
     ctot += s_wtot[w];
   }
@@ -432,16 +460,10 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   const int sh = (int)((reinterpret_cast<uintptr_t>(a.col_idx + wstart) >> 2) & 3u);
   const bool staged = a.values == nullptr && wtot + 3 <= kWarpBuf && wstart + wtot <= a.col_capacity;
   int32_t* wbuf = s_buf_all + warp * kWarpBuf;
-  if (cnt > 0) {
-    const bool unit_values = a.state->nonunit == 0;
-    const float* row = a.S + grow * a.K;
-    const bool fits = staged || pos + cnt <= a.col_capacity;
-    int32_t* dst = staged ? wbuf + sh + (incl - cnt) : a.col_idx + (fits ? pos : 0);
-    float* vdst = a.values ? a.values + (fits ? pos : 0) : nullptr;
-    int k = 0;
-    bool overflow = false;
+  // Calls emit(col) for the set columns of chunks [c0, c1) in ascending order.
+  auto expand = [&](auto&& emit) {
     for (int c = c0; c < c1; ++c) {
-      uint2 pw;
+      uint2 pw = make_uint2(0u, 0u);
       if (c - c0 < kPre) {
 #pragma unroll
         for (int e = 0; e < kPre; ++e)
@@ -460,36 +482,34 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
       for (int h = 0; h < 2; ++h) {
         uint32_t bits = words[h];
         const int cb = 64 * c + 32 * h;
-        if (fits) {
-          if (vdst == nullptr) {
-            while (bits) {
-              dst[k++] = cb + __ffs(bits) - 1;
-              bits &= bits - 1u;
-            }
-          } else {
-            while (bits) {
-              const int col = cb + __ffs(bits) - 1;
-              bits &= bits - 1u;
-              dst[k] = col;
-              vdst[k++] = unit_values ? 1.0f : row[col];
-            }
-          }
-        } else {
-          while (bits) {
-            const int col = cb + __ffs(bits) - 1;
-            bits &= bits - 1u;
-            const int64_t p = pos + k++;
-            if (p < a.col_capacity) {
-              a.col_idx[p] = col;
-              if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
-            } else {
-              overflow = true;
-            }
-          }
+        while (bits) {
+          emit(cb + __ffs(bits) - 1);
+          bits &= bits - 1u;
         }
       }
     }
-    if (overflow) report_device_error(SPK_DEV_CSR_OVERFLOW);
+  };
+  if (cnt > 0) {
+    if (staged) {
+      // shared-memory staging (a shared pointer throughout: no generic stores)
+      int32_t* sdst = wbuf + sh + (incl - cnt);
+      expand([&](int col) { *sdst++ = col; });
+    } else {
+      const bool unit_values = a.state->nonunit == 0;
+      const float* row = a.S + grow * a.K;
+      int64_t p = pos;
+      bool overflow = false;
+      expand([&](int col) {
+        if (p < a.col_capacity) {
+          a.col_idx[p] = col;
+          if (a.values) a.values[p] = unit_values ? 1.0f : row[col];
+        } else {
+          overflow = true;
+        }
+        ++p;
+      });
+      if (overflow) report_device_error(SPK_DEV_CSR_OVERFLOW);
+    }
   }
   if (staged) {
     __syncwarp();
