@@ -155,6 +155,24 @@ int spk_sparse_multistep_forward(const float* dense_input, int T, int64_t B, int
                                  int64_t col_capacity, float* output, int branch, void* workspace,
                                  size_t workspace_bytes, spk_stream_t stream);
 
+/* ------------------------------------------------------- linear + activation
+ * Y[r, n] = act(sum_k X[r, k] * W[k, n] + bias[n]) for X [R, K] fp32 row-major,
+ * W element (k, n) at W[k*w_stride_k + n*w_stride_n] (an nn.Linear weight
+ * [N, K]: w_stride_k = 1, w_stride_n = K), bias optional, Y [R, N] fp32:
+ *   SPK_ACT_NONE       y
+ *   SPK_ACT_HEAVISIDE  1 if y - thr > 0 else 0  (spike_fn(fc1(x) - threshold),
+ *                      attention.py:156; q, k spikes with thr = 0, :110-111)
+ *   SPK_ACT_VSPIKE     1 if (tanh(y) + 1) / 2 - thr > 0 else 0  (the v spikes
+ *                      with thr = tau[0], attention.py:112-115)
+ * fp32-accurate on the tensor cores (tf32 hi/lo splits of W and X).  Needs
+ * N > 64, K % 4 == 0 and a 16-byte aligned X.  Replaces the nn.Linear +
+ * threshold + Heaviside pairs around the spike-linear path. */
+enum { SPK_ACT_NONE = 0, SPK_ACT_HEAVISIDE = 1, SPK_ACT_VSPIKE = 2 };
+size_t spk_linear_act_workspace_bytes(int K, int N);
+int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n, int N,
+                   const float* bias, int act, float thr, float* Y, void* workspace, size_t workspace_bytes,
+                   spk_stream_t stream);
+
 /* ------------------------------------------------------- attention
  * apply_channel_decay (attention_cuda.cu:7-77, attention.py:30-44):
  * k_w[b, n, c] = k[b, n, c] * lam[c]^(N-1-n) over k [B_total, N, d]. */

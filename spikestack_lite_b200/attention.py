@@ -23,6 +23,16 @@ from .sparse import SparseLinear
 _attn_cuda_engine = attention_engine
 
 
+def engine_linear(lin, x, act="none", thr=0.0):
+    """act(lin(x)) through the engine's fp32-accurate tensor-core linear
+    (spk_linear_act) when autograd is off and the shape is one it takes
+    (out_features > 64, in_features % 4 == 0); None otherwise, and the caller
+    runs the module (the reference's own nn.Linear, which training needs)."""
+    if torch.is_grad_enabled() or not x.is_cuda or lin.out_features <= 64 or lin.in_features % 4:
+        return None
+    return ops.linear_act(x, lin.weight, lin.bias, act, thr)
+
+
 class SurrogateHeaviside(torch.autograd.Function):
     """(x > 0) forward, sigmoid-derivative surrogate backward (attention.py:13-24)."""
 
@@ -99,6 +109,10 @@ class AstrocyteHebbianAttention(nn.Module):
 
     def spikes(self, x):
         """q, k, v spike tensors of x (attention.py:110-118)."""
+        if self.L == 1:
+            q = engine_linear(self.q_proj, x, "heaviside")
+            if q is not None:  # v: (tanh(v_proj(x)) + 1) / 2 - tau[0] > 0, tau[0] = 1 / (L + 1)
+                return q, engine_linear(self.k_proj, x, "heaviside"), engine_linear(self.v_proj, x, "vspike", 0.5)
         q = spike_fn(self.q_proj(x))
         k = spike_fn(self.k_proj(x))
         u01 = (torch.tanh(self.v_proj(x)) + 1.0) / 2.0
@@ -129,7 +143,9 @@ class AstrocyteHebbianAttention(nn.Module):
         if x.device.type != "cuda":
             raise EngineError("AstrocyteHebbianAttention: CUDA input required (no CPU path)")
         q, k, v = self.spikes(x)
-        return self.o_proj(self.attend(q, k, v))
+        a = self.attend(q, k, v)
+        y = engine_linear(self.o_proj, a)
+        return y if y is not None else self.o_proj(a)
 
 
 class SpikingFFN(nn.Module):
@@ -147,7 +163,9 @@ class SpikingFFN(nn.Module):
             self.fc2 = nn.Linear(d_model * expansion, d_model)
 
     def forward(self, x):
-        act = spike_fn(self.fc1(x) - self.threshold)
+        act = engine_linear(self.fc1, x, "heaviside", self.threshold)
+        if act is None:
+            act = spike_fn(self.fc1(x) - self.threshold)
         if self.use_spikeskip and x.dim() == 4:
             return self.fc2.forward_multistep(act)
         return self.fc2(act)

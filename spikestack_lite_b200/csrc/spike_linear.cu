@@ -204,3 +204,36 @@ extern "C" int spk_sparse_multistep_forward(const float* dense_input, int T, int
   return reference_multistep(dense_input, T, B, I, weightT, O, nnz_per_row, row_offsets, col_indices, values,
                              col_capacity, output, branch, workspace, workspace_bytes, (cudaStream_t)stream);
 }
+
+// ------------------------------------------------------------ linear + activation
+// Y = act(X W^T + bias) for the projections around the path (the SpikingFFN
+// fc1 with its threshold spike, attention.py:156; the q/k/v spikes and the
+// o_proj of the attention, attention.py:110-118, 136).  fp32-accurate on the
+// tensor cores: W tf32 hi + lo, X rounded to tf32 in shared memory with its
+// remainder in a second pass (~2^-22 relative per product, as fp32).
+extern "C" size_t spk_linear_act_workspace_bytes(int K, int N) {
+  if (K < 1 || N < 1) return 0;
+  return spk::align_up(spk::tf32_img_bytes(spk::tc_plan(K, N, SPK_F32)), 1024);
+}
+
+extern "C" int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k,
+                              int64_t w_stride_n, int N, const float* bias, int act, float thr, float* Y,
+                              void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  using namespace spk;
+  SPK_REQUIRE(R >= 0 && K >= 1 && N >= 1, "bad shape R=%lld K=%d N=%d", (long long)R, K, N);
+  SPK_REQUIRE(W && (R == 0 || (X && Y)), "X, W and Y must be non-null");
+  SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_VSPIKE, "unknown activation %d", act);
+  SPK_REQUIRE(N > 64, "linear_act needs N > 64 (128-column tiles on the tensor cores)");
+  SPK_REQUIRE(K % 4 == 0 && (R == 0 || tc_supported(K, N, X)), "linear_act needs K %% 4 == 0 and a 16-byte aligned X");
+  const TcPlan p = tc_plan(K, N, SPK_F32);
+  const size_t need = align_up(tf32_img_bytes(p), 1024);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(SPK_EWORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  if (R == 0) return SPK_OK;
+  unsigned char* img = static_cast<unsigned char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch_w_image_tf32(W, w_stride_k, w_stride_n, K, N, p, img, nullptr, 0, st);
+  if (rc) return rc;
+  TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
+  return launch_wt(X, R, K, N, p, img, o, st, act, thr);
+}

@@ -85,6 +85,7 @@ struct TcArgs {
   int* nonunit;           // set to 1 when a positive value other than 1 is seen
   int32_t* blk_sum;       // spikes per 128-row block (for the CSR scan's prefixes)
   unsigned long long* sup_sum;  // spikes per 16384-row super-block
+  float thr;              // threshold of the spiking epilogues of the linear-activation op
 };
 
 template <int NT, bool WSPLIT>

@@ -98,8 +98,11 @@ __host__ __device__ __forceinline__ uint32_t sw128_chunk(uint32_t r, uint32_t c)
 // staging layout: 128 rows x 64 fp32 per slot, two 128-byte-swizzled atom
 // columns).  Warp cw of CW = 16 screens rows [8cw, 8cw+8) of every slot,
 // rewrites them for the exact hi/lo pass when needed, and emits the planar
-// spike masks, row counts and block sums of the CSR pass.
-template <int NS, int G>
+// spike masks, row counts and block sums of the CSR pass.  kRelu: the
+// spike-linear predicate relu'(x) (x if x > 0, else 0) is applied to S; the
+// linear-activation op passes its input through unchanged (hi = x rounded
+// to tf32, lo = the remainder).
+template <int NS, int G, bool kRelu = true>
 __device__ __forceinline__ void tf32_converter(const int cw, const int lane, unsigned char* stg, uint64_t* stg_full,
                                                uint64_t* chk, uint64_t* stg_empty, uint64_t* lo_go,
                                                uint64_t* lo_full, uint8_t* lo_flag, int* row_count,
@@ -177,7 +180,7 @@ __device__ __forceinline__ void tf32_converter(const int cw, const int lane, uns
             float h[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float xr = x[e] > 0.0f ? x[e] : 0.0f;
+              const float xr = (!kRelu || x[e] > 0.0f) ? x[e] : 0.0f;
               h[e] = tf32_rna(xr);
               lo_v[i][e] = isfinite(xr) ? tf32_rna(xr - h[e]) : 0.0f;
             }

@@ -74,6 +74,22 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// Epilogue of the weights-in-TMEM kernel, per element y = D + bias[n].
+enum WtEpilogue : int {
+  kEpiLinear = 0,     // y
+  kEpiHeaviside = 1,  // 1 if y - thr > 0 else 0 (spike_fn(fc1(x) - thr); q, k spikes with thr = 0)
+  kEpiVSpike = 2      // 1 if (tanh(y) + 1) / 2 - thr > 0 else 0 (the v spikes, thr = tau)
+};
+
+template <int kEpi>
+__device__ __forceinline__ float wt_epilogue(float y, float thr) {
+  if (kEpi == kEpiHeaviside) return (y - thr > 0.0f) ? 1.0f : 0.0f;
+  if (kEpi == kEpiVSpike) return ((tanhf(y) + 1.0f) / 2.0f - thr > 0.0f) ? 1.0f : 0.0f;
+  return y;
+}
+
+// kRelu: spike-linear (relu'(S)); false: the linear-activation op (plain X).
+template <int kEpi, bool kRelu>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
   constexpr int G = wt::kG, NS = wt::kNS, NP = wt::kNP, CW = wt::kConvWarps;
@@ -268,7 +284,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
         mbar_wait(&pc_full[i % NP], (i / NP) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
     }
   } else if (warp < 3 + CW) {
-    tf32_converter<NS, G>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count, abort_flag,
+    tf32_converter<NS, G, kRelu>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count, abort_flag,
                           a, r_begin, r_end, n_tile, nk, groups, tiles);
   } else {
     // ---------------------------------------------------------------- weight loaders + epilogue (warps 19-22)
@@ -331,7 +347,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
             float* y = a.Y + (row0 + rb) * a.N + n;
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj)
-              if (row0 + rb + jj < r_end) y[(int64_t)jj * a.N] = v[jj] + bias_n;
+              if (row0 + rb + jj < r_end) y[(int64_t)jj * a.N] = wt_epilogue<kEpi>(v[jj] + bias_n, a.thr);
           }
         }
       }
@@ -353,8 +369,24 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 // The weight image is the tf32 kernel's (tf32_img_bytes, w_image_tf32_kernel)
 // with NT = 128: per N tile and K chunk the pieces hi k0-31 | hi k32-63 |
 // lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle.
+template <int kEpi, bool kRelu>
+int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
+  auto kern = spike_linear_wt_kernel<kEpi, kRelu>;
+  SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wt::kSmemBytes));
+  const int64_t gx = ceil_div(a.R, a.rows_per_cta);
+  dim3 grid((unsigned)gx, (unsigned)n_tiles);
+  prof_before(SPK_KERNEL_DENSE, stream);
+  SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(wt::kThreads), wt::kSmemBytes, stream, map, a));
+  prof_after(SPK_KERNEL_DENSE, stream);
+  SPK_LAUNCH_CHECK();
+  count_launch(1);
+  return SPK_OK;
+}
+
+// act < 0: spike-linear (relu'(S) with the CSR outputs of `o`); act >= 0: the
+// linear-activation op with epilogue `act` (WtEpilogue) and threshold `thr`.
 int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
-              cudaStream_t stream) {
+              cudaStream_t stream, int act = -1, float thr = 0.0f) {
   if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
   CUtensorMap map;
   int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
@@ -374,19 +406,18 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.nonunit = o.nonunit;
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
-  SPK_CUDA_TRY(cudaFuncSetAttribute(spike_linear_wt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)wt::kSmemBytes));
+  a.thr = thr;
   const int sms = sm_count();
   const int ranges = sms / p.n_tiles > 0 ? sms / p.n_tiles : 1;
   a.rows_per_cta = ceil_div(ceil_div(a.R, ranges), 32) * 32;
-  const int64_t gx = ceil_div(a.R, a.rows_per_cta);
-  dim3 grid((unsigned)gx, (unsigned)p.n_tiles);
-  prof_before(SPK_KERNEL_DENSE, stream);
-  SPK_CUDA_TRY(launch_dependent(spike_linear_wt_kernel, grid, dim3(wt::kThreads), wt::kSmemBytes, stream, map, a));
-  prof_after(SPK_KERNEL_DENSE, stream);
-  SPK_LAUNCH_CHECK();
-  count_launch(1);
-  return SPK_OK;
+  switch (act) {
+    case -1: return launch_wt_inst<kEpiLinear, true>(map, a, p.n_tiles, stream);
+    case kEpiLinear: return launch_wt_inst<kEpiLinear, false>(map, a, p.n_tiles, stream);
+    case kEpiHeaviside: return launch_wt_inst<kEpiHeaviside, false>(map, a, p.n_tiles, stream);
+    case kEpiVSpike: return launch_wt_inst<kEpiVSpike, false>(map, a, p.n_tiles, stream);
+    default: break;
+  }
+  return fail(SPK_EINVAL, "unknown activation %d", act);
 }
 
 }  // namespace spk

@@ -14,7 +14,7 @@ import torch.nn as nn
 
 from . import ops
 from ._lib import EngineError
-from .attention import SurrogateHeaviside
+from .attention import SurrogateHeaviside, engine_linear
 from .engine import gsmc_engine
 
 _gsmc_cuda_engine = gsmc_engine
@@ -50,13 +50,16 @@ class FusedGSMC(nn.Module):
             raise EngineError("FusedGSMC: CUDA input required (no CPU path)")
         T_len, B, N, d = x.shape
         flat = x.reshape(T_len, -1, d)
-        gi_all = self.W_in(flat)
-        wd_all = self.W_d(flat)
         if not self.training and not torch.is_grad_enabled():
+            # input projections on the engine's tensor-core linear when it takes the shape
+            gi_all = engine_linear(self.W_in, flat)
+            gi_all = self.W_in(flat) if gi_all is None else gi_all
+            wd_all = engine_linear(self.W_d, flat)
+            wd_all = self.W_d(flat) if wd_all is None else wd_all
             pooled = ops.gsmc_forward(gi_all, wd_all, self.W_rec.weight, self.W_in.bias, self.v_th, self.gate_scale,
                                       self.adaptive_threshold, self.beta_adapt, self.pool)
             return pooled.view(B, N, d)
-        return self._forward_autograd(gi_all, wd_all, B, N, d, T_len)
+        return self._forward_autograd(self.W_in(flat), self.W_d(flat), B, N, d, T_len)
 
     def _forward_autograd(self, gi_all, wd_all, B, N, d, T_len):
         M = B * N

@@ -100,6 +100,40 @@ def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=Non
     return Y[0] if squeeze else Y
 
 
+_ACTS = {"none": 0, "heaviside": 1, "vspike": 2}
+
+
+def linear_act(x, weight, bias=None, act="none", thr=0.0):
+    """act(x @ weight.T + bias) for x [..., K] fp32 and an nn.Linear weight
+    [N, K] fp32 on the tensor cores, fp32-accurate (spk_linear_act):
+
+      "none"       y
+      "heaviside"  (y - thr > 0).float()               spike_fn(fc1(x) - thr); q, k spikes (thr 0)
+      "vspike"     ((tanh(y) + 1) / 2 - thr > 0).float()  v spikes (thr = tau)
+
+    Needs N > 64 and K % 4 == 0."""
+    require_cuda(x, weight, bias, what="linear_act")
+    require_f32(x, weight, bias, what="linear_act")
+    if act not in _ACTS:
+        raise EngineError(f"linear_act: act must be one of {sorted(_ACTS)}")
+    x = _contig(x)
+    K = x.shape[-1]
+    N, Kw = weight.shape
+    if Kw != K:
+        raise EngineError(f"linear_act: weight K={Kw} does not match input K={K}")
+    if bias is not None:
+        bias = _contig(bias)
+        if bias.numel() != N:
+            raise EngineError("linear_act: bias must have N elements")
+    R = x.numel() // K if K else 0
+    Y = torch.empty(*x.shape[:-1], N, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(x.device, lib.spk_linear_act_workspace_bytes(K, N))
+    check(lib.spk_linear_act(ptr(x), R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(bias),
+                             _ACTS[act], float(thr), ptr(Y), ws, wsn, stream_of(x)), "spk_linear_act")
+    return Y
+
+
 def alloc_csr(T, M, K, device, capacity=None, values=False):
     """Preallocated per-plane CSR buffers for spike_linear(csr=...)."""
     cap = int(capacity if capacity is not None else T * M * K)

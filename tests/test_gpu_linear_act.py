@@ -1,0 +1,102 @@
+"""Linear + activation on the tensor cores (spk_linear_act) against fp64.
+
+The projections around the spike-linear path (SpikingFFN fc1 + threshold
+spike, attention q/k/v spikes, o_proj) are fp32 nn.Linear layers in the
+reference.  The engine computes them fp32-accurate (tf32 hi/lo splits of both
+operands): outputs within 1e-5 x max|ref| of the fp64 product, and no less
+accurate than the cuBLAS fp32 GEMM; spikes equal to the fp64 decision except
+where the pre-activation lies within rounding distance of the threshold."""
+import pytest
+import torch
+
+from spikestack_lite_b200 import ops
+from spikestack_lite_b200._lib import EngineError
+
+pytestmark = pytest.mark.gpu
+
+
+def _data(R, K, N, seed, bias=True):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(R, K, generator=g, device="cuda")
+    w = torch.randn(N, K, generator=g, device="cuda") / K ** 0.5
+    b = torch.randn(N, generator=g, device="cuda") * 0.1 if bias else None
+    return x, w, b
+
+
+def _ref64(x, w, b):
+    y = x.double() @ w.double().t()
+    return y + b.double() if b is not None else y
+
+
+@pytest.mark.parametrize("R,K,N,bias", [
+    (1000, 512, 2048, True),    # fc1 geometry (d 512 -> 4d)
+    (4096, 512, 512, True),     # q/k/v/o projection geometry
+    (257, 96, 300, False),      # partial row tile, partial N tile, K not a multiple of 64
+    (3, 4, 65, True),           # smallest K, N just above the narrow-N limit
+])
+def test_linear_fp32_accuracy(R, K, N, bias):
+    x, w, b = _data(R, K, N, seed=R + K + N, bias=bias)
+    y = ops.linear_act(x, w, b)
+    ref = _ref64(x, w, b)
+    scale = ref.abs().max().item()
+    err = (y.double() - ref).abs().max().item()
+    cublas = torch.nn.functional.linear(x, w, b)
+    err_cublas = (cublas.double() - ref).abs().max().item()
+    assert err <= max(1e-5 * scale, 4 * err_cublas), (err, err_cublas, scale)
+
+
+def test_real_world_scale_inputs():
+    # wide dynamic range and negative values (no relu on this op)
+    x, w, b = _data(512, 256, 384, seed=7)
+    x = x * torch.logspace(-3, 3, 256, device="cuda")
+    y = ops.linear_act(x, w, b)
+    ref = _ref64(x, w, b)
+    assert (y.double() - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("thr", [0.0, 0.25])
+def test_heaviside_spikes(thr):
+    x, w, b = _data(2048, 512, 2048, seed=11)
+    s = ops.linear_act(x, w, b, act="heaviside", thr=thr)
+    pre = _ref64(x, w, b) - thr
+    want = (pre > 0).float()
+    near = pre.abs() < 1e-5 * pre.abs().max()
+    assert set(s.unique().tolist()) <= {0.0, 1.0}
+    assert torch.equal(s[~near], want[~near])
+    # the reference op on the GPU (cuBLAS fp32 + threshold): flips only near the threshold
+    ref_gpu = ((torch.nn.functional.linear(x, w, b) - thr) > 0).float()
+    assert (s != ref_gpu).float().mean().item() < 1e-4
+
+
+def test_vspike():
+    x, w, b = _data(1024, 512, 512, seed=13)
+    tau = 0.5
+    s = ops.linear_act(x, w, b, act="vspike", thr=tau)
+    y = _ref64(x, w, b)
+    u = (torch.tanh(y) + 1.0) / 2.0 - tau
+    want = (u > 0).float()
+    near = u.abs() < 1e-5
+    assert torch.equal(s[~near], want[~near])
+
+
+def test_leading_dims_and_empty():
+    x, w, b = _data(4 * 3 * 50, 128, 256, seed=17)
+    x4 = x.view(4, 3, 50, 128)
+    y4 = ops.linear_act(x4, w, b)
+    assert y4.shape == (4, 3, 50, 256)
+    torch.testing.assert_close(y4.view(-1, 256), ops.linear_act(x, w, b), rtol=0, atol=0)
+    e = ops.linear_act(torch.empty(0, 128, device="cuda"), w, b)
+    assert e.shape == (0, 256)
+
+
+def test_rejects_unsupported():
+    x, w, b = _data(8, 128, 64, seed=19)
+    with pytest.raises(EngineError):
+        ops.linear_act(x, w, b)                                   # N <= 64
+    x, w, b = _data(8, 126, 128, seed=21)
+    with pytest.raises(EngineError):
+        ops.linear_act(x, w, b)                                   # K % 4 != 0
+    with pytest.raises(EngineError):
+        ops.linear_act(x.cpu(), w.cpu(), None)                    # no CPU path
+    with pytest.raises(EngineError):
+        ops.linear_act(x, w, b, act="relu")
