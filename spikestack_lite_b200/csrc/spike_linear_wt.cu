@@ -44,7 +44,6 @@ constexpr int kBoxBytes = kBoxRows * 128;
 constexpr int kPieceBytes = kLanes * 128;   // 128 n x 32 k of hi or lo: 16 KB
 constexpr int kPieces = 4;                  // per 64-wide K chunk: hi k0-31, hi k32-63, lo k0-31, lo k32-63
 constexpr int kConvWarps = t32::kConvWarps;
-constexpr int kNS = 5;                      // staging slots
 constexpr int kNP = 4;                      // weight-piece slots
 constexpr int kG = 2;                       // row tiles per accumulator group
 constexpr int kWarps = 3 + kConvWarps + 4;
@@ -52,12 +51,20 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 columns
 constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
-constexpr size_t kRing = (size_t)kNS * kStgBytes + (size_t)kNP * kPieceBytes;
-// barriers (5 NS + 2 NP + 7), lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
-constexpr size_t kTail = 8 * (5 * kNS + 2 * kNP + 7) + kConvWarps * kNS + 4 * kRows * kG + 16;
-static_assert((8 * (5 * kNS + 2 * kNP + 7)) % 16 == 0, "lo flags 16-byte aligned");
-constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+// Shared-memory rings per mode.  Spike-linear: five S slots.  Linear op:
+// three X slots and two remainder buffers (the X slot itself is the hi part).
+template <bool kRelu>
+struct Ring {
+  static constexpr int NS = kRelu ? 5 : 3;  // staging slots
+  static constexpr int NL = kRelu ? 0 : 2;  // remainder buffers
+  static constexpr size_t kRing = (size_t)(NS + NL) * kStgBytes + (size_t)kNP * kPieceBytes;
+  // barriers, lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
+  static constexpr int kBars = 5 * NS + 2 * NL + 2 * kNP + 7;
+  static constexpr size_t kTail = 8 * kBars + kConvWarps * NS + 4 * kRows * kG + 16;
+  static constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
+  static_assert((8 * kBars) % 16 == 0, "lo flags 16-byte aligned");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
 static_assert(kDcol + kG * kRows <= kTmemCols && kAcol + 2 * 2 * kKChunk <= kDcol, "TMEM budget");
 static_assert(kRows == t32::kRows && kStgBytes == t32::kStgBytes, "staging layout shared with the converters");
 
@@ -88,15 +95,74 @@ __device__ __forceinline__ float wt_epilogue(float y, float thr) {
   return y;
 }
 
+// Converter warps of the linear op.  The tensor core reads the X slot's fp32
+// values truncated to tf32 (the hi part); each warp reads its 8 rows once and
+// writes their remainders x - trunc(x) (exact in fp32; ~2^-21 relative after
+// the tensor core truncates them in turn) into a remainder buffer of the same
+// layout.  The slot itself is never rewritten, so a warp never waits for the
+// MMAs inside a slot, only for a free remainder buffer.
+template <int NS, int NL, int G>
+__device__ __forceinline__ void linear_converter(const int cw, const int lane, unsigned char* stg,
+                                                 unsigned char* lob, uint64_t* stg_full, uint64_t* stg_empty,
+                                                 uint64_t* lof, uint64_t* loe, volatile int* abort_flag,
+                                                 const int64_t r_begin, const int64_t r_end, const int nk,
+                                                 const int groups, const int tiles) {
+  constexpr int RPW = wt::kRows / wt::kConvWarps;  // rows per converter warp
+  constexpr int NLD = RPW / 2;                      // 16-byte loads per lane and slot
+  const int half = lane >> 4, cl = lane & 15;
+  uint32_t soff[NLD];
+  int rls[NLD];
+#pragma unroll
+  for (int i = 0; i < NLD; ++i) {
+    rls[i] = cw * RPW + 2 * i + half;
+    soff[i] = (uint32_t)((cl >> 3) * wt::kAtomBytes) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
+  }
+  auto rem = [](uint32_t b) -> float {
+    const float x = __uint_as_float(b);
+    return isinf(x) ? 0.0f : x - __uint_as_float(b & 0xffffe000u);  // NaN stays NaN
+  };
+  int j = 0;
+  bool ok = true;
+  for (int g = 0; g < groups && ok; ++g) {
+    const int tg = min(G, tiles - g * G);
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      for (int t = 0; t < tg; ++t, ++j) {
+        const int s = j % NS, l = j % NL;
+        if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(g * G + t) * wt::kRows));
+        const unsigned char* st = stg + s * wt::kStgBytes;
+        float4 lo[NLD];
+#pragma unroll
+        for (int i = 0; i < NLD; ++i) {
+          const uint4 b = rls[i] < nrows ? *reinterpret_cast<const uint4*>(st + soff[i]) : make_uint4(0u, 0u, 0u, 0u);
+          lo[i] = make_float4(rem(b.x), rem(b.y), rem(b.z), rem(b.w));
+        }
+        if (j >= NL && !(ok = mbar_wait(&loe[l], ((j / NL) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        unsigned char* lb = lob + l * wt::kStgBytes;
+#pragma unroll
+        for (int i = 0; i < NLD; ++i) *reinterpret_cast<float4*>(lb + soff[i]) = lo[i];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&lof[l]);
+          mbar_arrive(&stg_empty[s]);  // this warp has read the slot
+        }
+      }
+    }
+  }
+}
+
 // kRelu: spike-linear (relu'(S)); false: the linear-activation op (plain X).
 template <int kEpi, bool kRelu>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
-  constexpr int G = wt::kG, NS = wt::kNS, NP = wt::kNP, CW = wt::kConvWarps;
+  using RG = wt::Ring<kRelu>;
+  constexpr int G = wt::kG, NS = RG::NS, NL = RG::NL, NP = wt::kNP, CW = wt::kConvWarps;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
-  unsigned char* pcs = stg + NS * wt::kStgBytes;              // [NP][16 KB] weight pieces
+  unsigned char* lob = stg + NS * wt::kStgBytes;              // [NL][32 KB] remainders (linear op)
+  unsigned char* pcs = lob + NL * wt::kStgBytes;              // [NP][16 KB] weight pieces
   uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes);
   uint64_t* stg_full = bars;
   uint64_t* chk = stg_full + NS;
@@ -110,7 +176,9 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
-  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(drain + 1);       // [NS][CW] bytes, 16-byte aligned
+  uint64_t* lof = drain + 1;   // [NL] remainder buffer written (linear op)
+  uint64_t* loe = lof + NL;    // [NL] remainder buffer read by the MMAs
+  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(loe + NL);        // [NS][CW] bytes, 16-byte aligned
   int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -143,6 +211,10 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
     mbar_init(drain, 1);
+    for (int l = 0; l < NL; ++l) {
+      mbar_init(&lof[l], CW);
+      mbar_init(&loe[l], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -223,6 +295,31 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           const uint32_t a_lo = a_hi + 64u;
           for (int t = 0; t < tg; ++t) {
             const int s = j % NS;
+            if constexpr (!kRelu) {
+              // linear op: hi = the slot as the tensor core reads it, lo = the
+              // remainder buffer; both passes back to back
+              const int l = j % NL;
+              if (!(ok = mbar_wait(&lof[l], (j / NL) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+              tc_fence_after();
+              const uint32_t d = tmem + wt::kDcol + (uint32_t)(t * wt::kRows);
+              const uint64_t db0 = umma_desc_sw128_kmajor(smem_u32(stg + s * wt::kStgBytes));
+              const uint64_t dl0 = umma_desc_sw128_kmajor(smem_u32(lob + l * wt::kStgBytes));
+#pragma unroll
+              for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
+                const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
+                umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db0 + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                umma_tf32_ts(d, a_lo + (uint32_t)kk * 8u, db0 + off, idesc, 1u);
+              }
+#pragma unroll
+              for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
+                const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
+                umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, dl0 + off, idesc, 1u);
+              }
+              umma_commit(&stg_empty[s]);
+              umma_commit(&loe[l]);
+              ++j;
+              continue;
+            }
             if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
             tc_fence_after();
             const uint4 lf = *reinterpret_cast<const uint4*>(lo_flag + s * CW);  // the 16 warps' flags
@@ -284,8 +381,13 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
         mbar_wait(&pc_full[i % NP], (i / NP) & 1, nullptr, SPK_DEV_PIPE_TIMEOUT);
     }
   } else if (warp < 3 + CW) {
-    tf32_converter<NS, G, kRelu>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count, abort_flag,
-                          a, r_begin, r_end, n_tile, nk, groups, tiles);
+    if constexpr (!kRelu) {
+      linear_converter<NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, abort_flag, r_begin, r_end,
+                                  nk, groups, tiles);
+    } else {
+      tf32_converter<NS, G, kRelu>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count,
+                                   abort_flag, a, r_begin, r_end, n_tile, nk, groups, tiles);
+    }
   } else {
     // ---------------------------------------------------------------- weight loaders + epilogue (warps 19-22)
     // Warp q = warp & 3 owns TMEM lanes [32q, 32q+32): output columns n0 + 32q + lane.
@@ -372,11 +474,12 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 template <int kEpi, bool kRelu>
 int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
   auto kern = spike_linear_wt_kernel<kEpi, kRelu>;
-  SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wt::kSmemBytes));
+  constexpr size_t smem = wt::Ring<kRelu>::kSmemBytes;
+  SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t gx = ceil_div(a.R, a.rows_per_cta);
   dim3 grid((unsigned)gx, (unsigned)n_tiles);
   prof_before(SPK_KERNEL_DENSE, stream);
-  SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(wt::kThreads), wt::kSmemBytes, stream, map, a));
+  SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(wt::kThreads), smem, stream, map, a));
   prof_after(SPK_KERNEL_DENSE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
