@@ -61,6 +61,21 @@ def test_cpu_inputs_raise_instead_of_falling_back():
         SparseLinear(1024, 16)(torch.zeros(2, 1024))
 
 
+def test_linear_act_host_checks():
+    from spikestack_lite_b200 import ops
+    from spikestack_lite_b200.attention import engine_linear
+
+    x, w = torch.randn(4, 128), torch.randn(256, 128)
+    with pytest.raises(EngineError, match="CUDA"):
+        ops.linear_act(x, w)
+    # autograd on, or a CPU input: the module's own nn.Linear runs (None = not taken)
+    lin = torch.nn.Linear(128, 256)
+    assert engine_linear(lin, x) is None
+    with torch.no_grad():
+        assert engine_linear(lin, x) is None                  # CPU input
+        assert engine_linear(torch.nn.Linear(128, 64), x) is None  # narrow N
+
+
 def test_unsupported_stems_are_rejected():
     with pytest.raises(EngineError):
         SpikingTransformer(use_conv_stem=True)
