@@ -9,7 +9,7 @@ Metric: GSOP/s, SOP = one (nonzero input spike, output neuron) accumulate,
 SOPs per step = nnz(S) * N.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spike_linear|sweep|attention|model_small|model_full]
+                    [--workload spike_linear|sweep|attention|linear|model_small|model_full]
 
 N > 1: launched by torchrun, one rank per GPU; every rank runs its own
 instance (the rows are independent -> weak scaling, no collective on the data
@@ -412,6 +412,77 @@ def run_attention(args, dist, cfg):
                          "frac": round(bytes_ / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}}
 
 
+# ------------------------------------------------------------ linear + activation
+# tcgen05 kind::tf32 rate on one SM, measured with back-to-back 128x128x8 MMAs
+# (A in TMEM, B in shared memory): 4096 FLOP per clock.
+TF32_FLOP_PER_CLK_SM = 4096
+
+
+def run_linear(args, dist, cfg):
+    """The C5 SpikingFFN fc1 with its threshold spike: act = (x W1^T + b - thr > 0)
+    over x [T*B*N, d] (ops.linear_act, three tf32 passes for fp32 accuracy)."""
+    from spikestack_lite_b200 import _lib, ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    R, K, N = cfg["R"], cfg["K"], cfg["N"]
+    if args.batch is not None:
+        R = args.batch * cfg["rows_per_batch"]
+    g = torch.Generator(device=dev).manual_seed(11 + dist.rank)
+    x = torch.randn(R, K, generator=g, device=dev)
+    w = torch.randn(N, K, generator=g, device=dev) / K ** 0.5
+    b = torch.randn(N, generator=g, device=dev) * 0.1
+    out = torch.empty(R, N, device=dev)
+
+    def step():
+        return ops.linear_act(x, w, b, act="heaviside", thr=cfg["thr"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if args.quick:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return {"workload": cfg["name"], "quick": True, "steps": args.steps}
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            out = step()
+        stop.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = dist.max(start.elapsed_time(stop)) / args.steps
+    _lib.profile_begin("dense")
+    for _ in range(max(3, args.steps // 2)):
+        step()
+    tot, n = _lib.profile_end()
+    kms = tot / max(n, 1)
+    # parity spot check: spikes of 256 rows against the fp64 decision away from the threshold
+    pre = (x[:256].double() @ w.double().t() + b.double()) - cfg["thr"]
+    near = pre.abs() < 1e-5 * pre.abs().max()
+    mism = int(((out[:256] > 0) != (pre > 0))[~near].sum().item())
+    flops = 2.0 * R * K * N                      # the fp32 GEMM's FLOPs
+    tf32_work = 3 * flops                        # three tf32 passes
+    clk = clocks.summary().get("sm_mhz") or 1965.0
+    peak_tf32 = TF32_FLOP_PER_CLK_SM * 148 * clk * 1e6 / 1e12
+    ach = tf32_work / (kms / 1e3) / 1e12
+    return {"metric": METRIC, "value": round(dist.world * flops / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s (fp32 GEMM)",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "R": R, "K": K, "N": N, "thr": cfg["thr"],
+                       "timing": "eager steps (weight image + linear kernel), CUDA events, max over ranks"},
+            "kernel_ms": {"linear": round(kms, 4)},
+            "roofline": {"kernel": "spike_linear_wt_kernel<heaviside>", "bound": "tensor",
+                         "achieved": round(ach, 1), "peak": round(peak_tf32, 1), "unit": "TFLOP/s (tf32)",
+                         "frac": round(ach / peak_tf32, 4), "alg_flops_per_launch": tf32_work, "traffic": None,
+                         "peak_src": "tcgen05 tf32 probe rate x 148 SMs x median SM clock"},
+            "parity_spike_mismatches": mism, "clocks": clocks.summary()}
+
+
 # ------------------------------------------------------------------- model
 def run_model(args, dist, cfg):
     from spikestack_lite_b200.transformer import SpikingTransformer
@@ -459,6 +530,8 @@ WORKLOADS = {
                      "T": 3, "M": 16384, "K": 512, "N": 128, "p": 0.10, "w_dtype": "f32", "csr": True},
     "sweep": {"name": "spike-linear density sweep S[4,65536,2048], W[2048,2048] bf16", "T": 4, "M": 65536,
               "K": 2048, "N": 2048, "p": 0.10, "w_dtype": "bf16", "csr": False},
+    "linear": {"name": "C5 SpikingFFN fc1 + threshold spike: x[4*512*1024, 512] -> [.., 2048]", "R": 4 * 512 * 1024,
+               "rows_per_batch": 4 * 1024, "K": 512, "N": 2048, "thr": 0.0},
     "attention": {"name": "spiking linear attention B=64 H=8 L=4096 dh=64 T=4 p=0.15", "T": 4, "B": 64,
                   "L": 4096, "H": 8, "dh": 64, "p": 0.15},
     "model_small": {"name": "SpikingTransformer fwd, batch 256, seq 64, d 128, 1 layer, T=3", "batch": 256,
@@ -516,6 +589,8 @@ def main():
             res = run_spike_linear(args, dist, cfg)
         elif args.workload == "attention":
             res = run_attention(args, dist, cfg)
+        elif args.workload == "linear":
+            res = run_linear(args, dist, cfg)
         else:
             res = run_model(args, dist, cfg)
         if dist.rank == 0:

@@ -79,8 +79,10 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
   const bool want_csr = row_ptr != nullptr || col_idx != nullptr || plane_ptr != nullptr;
   SPK_REQUIRE(!want_csr || (row_ptr && col_idx && plane_ptr), "CSR outputs need row_ptr, col_idx and plane_ptr");
   branch = resolve_branch(branch, K, N, S);
-  if (branch == SPK_BRANCH_DENSE)
+  if (branch == SPK_BRANCH_DENSE) {
     SPK_REQUIRE(tc_supported(K, N, S), "dense branch needs K %% 4 == 0 and a 16-byte aligned S");
+    SPK_REQUIRE((int64_t)T * M < (int64_t(1) << 31), "dense branch: T*M must stay below 2^31 rows (TMA coordinates)");
+  }
   const bool internal_csr = (branch == SPK_BRANCH_CSR) && !want_csr;
   const SlLayout L = sl_layout(T, M, K, N, w_dtype, internal_csr);
   if (ws == nullptr || ws_bytes < L.total)
@@ -221,6 +223,7 @@ extern "C" int spk_linear_act(const float* X, int64_t R, int K, const float* W, 
                               void* workspace, size_t workspace_bytes, spk_stream_t stream) {
   using namespace spk;
   SPK_REQUIRE(R >= 0 && K >= 1 && N >= 1, "bad shape R=%lld K=%d N=%d", (long long)R, K, N);
+  SPK_REQUIRE(R < (int64_t(1) << 31), "linear_act: at most 2^31 - 1 rows per call (TMA row coordinates)");
   SPK_REQUIRE(W && (R == 0 || (X && Y)), "X, W and Y must be non-null");
   SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_VSPIKE, "unknown activation %d", act);
   SPK_REQUIRE(N > 64, "linear_act needs N > 64 (128-column tiles on the tensor cores)");
