@@ -41,8 +41,12 @@ class SpireEncoder(nn.Module):
         v = (u - self.frontier.view(1, 1, self.d_model) - self.temporal_frontier).float()
         if self.n_repeats == 1 and not self.temporal:
             return spike_fn(v)
-        planes = spike_fn(v.unsqueeze(-1) - self.dither.float()).permute(3, 0, 1, 2)
-        return planes if self.temporal else planes.mean(dim=0)
+        if self.temporal:
+            # the planes (R, B, N, d) laid out contiguously: the reference's
+            # permute of the (B, N, d, R) comparison has the same values but
+            # leaves every later residual add and layer norm on a strided view
+            return spike_fn(v.unsqueeze(0) - self.dither.float().view(-1, 1, 1, 1))
+        return spike_fn(v.unsqueeze(-1) - self.dither.float()).permute(3, 0, 1, 2).mean(dim=0)
 
 
 class _LatencyHeadParams(nn.Module):
