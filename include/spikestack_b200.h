@@ -211,6 +211,18 @@ int spk_gsmc_forward(const float* gi_all, const float* wd_all, const float* w_re
                      int64_t M, int d, float v_th, float gate_scale, int adaptive, float beta, int pool_mean,
                      float* out_all, float* pooled, void* workspace, size_t workspace_bytes, spk_stream_t stream);
 
+/* ------------------------------------------------------- residual add + layer norm
+ * The pre-norm block's residual add and the layer norm of its result
+ * (AstrocyteHebbianBlock.forward, nn/attention.py:174-177: x + attn(norm1(x)),
+ * then norm2 of that sum; the block's output sum and the next block's norm1)
+ * in one pass, per row of width d:
+ *   H = X + D,  Y = (H - mean(H)) / sqrt(var(H) + eps) * gamma + beta,
+ * with the biased variance of nn.LayerNorm.  D null: Y = LayerNorm(X) and H
+ * is not written.  gamma / beta null: 1 / 0.  All pointers 16-byte aligned,
+ * d % 4 == 0, d <= 1024 (SPK_EUNSUPPORTED above); H may alias X. */
+int spk_add_layernorm(const float* X, const float* D, const float* gamma, const float* beta, int64_t rows, int d,
+                      float eps, float* H, float* Y, spk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

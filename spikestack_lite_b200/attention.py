@@ -33,6 +33,15 @@ def engine_linear(lin, x, act="none", thr=0.0):
     return ops.linear_act(x, lin.weight, lin.bias, act, thr)
 
 
+def _engine_norm_ok(norm, x):
+    """True when the engine's residual add + layer norm (spk_add_layernorm) can
+    stand in for `norm` on x: autograd off, CUDA fp32 input, a layer norm over
+    the last dimension of width d % 4 == 0, d <= 1024."""
+    d = x.shape[-1]
+    return (not torch.is_grad_enabled() and x.is_cuda and x.dtype == torch.float32
+            and tuple(norm.normalized_shape) == (d,) and d % 4 == 0 and d <= 1024)
+
+
 class SurrogateHeaviside(torch.autograd.Function):
     """(x > 0) forward, sigmoid-derivative surrogate backward (attention.py:13-24)."""
 
@@ -183,5 +192,20 @@ class AstrocyteHebbianBlock(nn.Module):
         self.ffn = SpikingFFN(d_model, expansion, use_spikeskip=use_spikeskip, spike_threshold=spike_threshold)
 
     def forward(self, x):
-        x = x + self.attn(self.norm1(x))
-        return x + self.ffn(self.norm2(x))
+        return self.forward_fused(x)[0]
+
+    def forward_fused(self, x, x_norm=None, next_norm=None):
+        """(block(x), next_norm(block(x)) or None).  At inference each residual
+        add runs together with the layer norm of its result (ops.add_layernorm):
+        x + attn(.) with norm2, and the block output with `next_norm` (the next
+        block's norm1), whose result the caller hands back as `x_norm`."""
+        if not _engine_norm_ok(self.norm1, x):  # the reference's composition (autograd, CPU)
+            x = x + self.attn(self.norm1(x))
+            return x + self.ffn(self.norm2(x)), None
+        if x_norm is None:
+            x_norm = ops.add_layernorm(x, None, self.norm1.weight, self.norm1.bias, self.norm1.eps)[1]
+        h, h_norm = ops.add_layernorm(x, self.attn(x_norm), self.norm2.weight, self.norm2.bias, self.norm2.eps)
+        f = self.ffn(h_norm)
+        if next_norm is None:
+            return h + f, None
+        return ops.add_layernorm(h, f, next_norm.weight, next_norm.bias, next_norm.eps)

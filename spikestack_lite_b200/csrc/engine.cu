@@ -10,4 +10,5 @@
 #include "attention.cu"
 #include "attention_tc.cu"
 #include "gsmc.cu"
+#include "layernorm.cu"
 #include "csr_noalloc.cu"

@@ -310,3 +310,32 @@ def gsmc_forward(gi_all, wd_all, w_rec, bias, v_th=1.0, gate_scale=4.0, adaptive
                                float(gate_scale), int(bool(adaptive)), float(beta), 1 if pool == "mean" else 0,
                                ptr(planes), ptr(pooled), ws, wsn, stream_of(gi_all)), "spk_gsmc_forward")
     return (pooled, planes) if return_planes else pooled
+
+
+# --------------------------------------------------------------------------- residual add + layer norm
+def add_layernorm(x, delta, weight=None, bias=None, eps=1e-5):
+    """h = x + delta and y = layer_norm(h) over the last dimension in one pass
+    (spk_add_layernorm): the pre-norm block's residual add followed by the
+    nn.LayerNorm of the sum (nn/attention.py:174-177).  delta None: h = x and
+    y = layer_norm(x).  weight / bias: the nn.LayerNorm affine parameters [d]
+    (None: 1 / 0).  Returns (h, y).  Needs d % 4 == 0 and d <= 1024."""
+    require_cuda(x, delta, weight, bias, what="add_layernorm")
+    require_f32(x, delta, weight, bias, what="add_layernorm")
+    x = _contig(x)
+    d = x.shape[-1]
+    if delta is not None:
+        if delta.shape != x.shape:
+            raise EngineError(f"add_layernorm: delta shape {tuple(delta.shape)} != x shape {tuple(x.shape)}")
+        delta = _contig(delta)
+    for name, p in (("weight", weight), ("bias", bias)):
+        if p is not None and p.numel() != d:
+            raise EngineError(f"add_layernorm: {name} must have d={d} elements")
+    weight = _contig(weight) if weight is not None else None
+    bias = _contig(bias) if bias is not None else None
+    rows = x.numel() // d if d else 0
+    h = torch.empty_like(x) if delta is not None else x
+    y = torch.empty_like(x)
+    check(_lib.load().spk_add_layernorm(ptr(x), ptr(delta), ptr(weight), ptr(bias), rows, d, float(eps),
+                                        ptr(h) if delta is not None else None, ptr(y), stream_of(x)),
+          "spk_add_layernorm")
+    return h, y

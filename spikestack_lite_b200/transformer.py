@@ -122,8 +122,10 @@ class SpikingTransformer(nn.Module):
         if x.device.type != "cuda":
             raise EngineError("SpikingTransformer: CUDA input required (no CPU path)")
         context = self.embedding(x)
-        for block in self.blocks:
-            context = block(context)
+        context_norm = None  # the next block's norm1 of the context, when the engine computed it
+        for i, block in enumerate(self.blocks):
+            nxt = self.blocks[i + 1].norm1 if i + 1 < len(self.blocks) else None
+            context, context_norm = block.forward_fused(context, context_norm, nxt)
         if self.gsmc is not None:
             context = self.gsmc(context, T=context.shape[0])
         self._pooled_for_latency = context.mean(dim=(0, 2)) if (self.temporal and self.gsmc is None) \

@@ -85,3 +85,17 @@ def test_python_ops_refuse_cpu_tensors(lib):
         ops.csr_compact(torch.zeros(2, 8))
     with pytest.raises(EngineError, match="CUDA"):
         ops.spiking_attention(*(torch.zeros(1, 4, 8) for _ in range(3)), torch.ones(8), 2)
+
+
+def test_add_layernorm_rejects_bad_arguments(lib):
+    from spikestack_lite_b200._lib import SPK_EINVAL, SPK_EUNSUPPORTED, SPK_OK
+
+    p = ctypes.c_void_p(256)
+    assert lib.spk_add_layernorm(None, None, None, None, 0, 512, 1e-5, None, None, None) == SPK_OK  # no rows
+    assert lib.spk_add_layernorm(p, None, None, None, 4, 510, 1e-5, None, p, None) == SPK_EINVAL
+    assert b"multiple of 4" in lib.spk_last_error()
+    assert lib.spk_add_layernorm(p, None, None, None, 4, 2048, 1e-5, None, p, None) == SPK_EUNSUPPORTED
+    assert lib.spk_add_layernorm(p, p, None, None, 4, 512, 1e-5, None, p, None) == SPK_EINVAL  # D without H
+    assert lib.spk_add_layernorm(ctypes.c_void_p(260), None, None, None, 4, 512, 1e-5, None, p, None) == SPK_EINVAL
+    assert b"aligned" in lib.spk_last_error()
+    assert lib.spk_add_layernorm(p, None, None, None, 4, 512, -1.0, None, p, None) == SPK_EINVAL

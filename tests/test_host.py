@@ -76,6 +76,24 @@ def test_linear_act_host_checks():
         assert engine_linear(torch.nn.Linear(128, 64), x) is None  # narrow N
 
 
+def test_add_layernorm_host_checks():
+    from spikestack_lite_b200 import ops
+    from spikestack_lite_b200.attention import AstrocyteHebbianBlock, _engine_norm_ok
+
+    x = torch.randn(2, 8, 128)
+    with pytest.raises(EngineError, match="CUDA"):
+        ops.add_layernorm(x, x)
+    ln = torch.nn.LayerNorm(128)
+    with torch.no_grad():
+        assert not _engine_norm_ok(ln, x)                      # CPU input: the reference's composition
+    # off the engine path the block runs the reference's composition, whose
+    # attention has no CPU path either
+    torch.manual_seed(0)
+    blk = AstrocyteHebbianBlock(d_model=128, num_heads=4)
+    with torch.no_grad(), pytest.raises(EngineError, match="CUDA"):
+        blk.forward_fused(x, None, blk.norm1)
+
+
 def test_unsupported_stems_are_rejected():
     with pytest.raises(EngineError):
         SpikingTransformer(use_conv_stem=True)
