@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* drain = acc_empty + 1;
   uint64_t* lof = drain + 1;   // [NL] remainder buffer written (linear op)
   uint64_t* loe = lof + NL;    // [NL] remainder buffer read by the MMAs
-  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(loe + NL);        // [NS][CW] bytes, 16-byte aligned
+  static_assert(5 * NS + 2 * NP + 7 + 2 * NL == RG::kBars, "the barriers above fill the barrier block");
+  uint8_t* lo_flag = reinterpret_cast<uint8_t*>(bars + RG::kBars);  // [NS][CW] bytes, 16-byte aligned
   int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
