@@ -9,7 +9,7 @@ Metric: GSOP/s, SOP = one (nonzero input spike, output neuron) accumulate,
 SOPs per step = nnz(S) * N.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spike_linear|sweep|attention|linear|model_small|model_full]
+                    [--workload spike_linear|sweep|attention|linear|layernorm|model_small|model_full]
 
 N > 1: launched by torchrun, one rank per GPU; every rank runs its own
 instance (the rows are independent -> weak scaling, no collective on the data
@@ -483,6 +483,60 @@ def run_linear(args, dist, cfg):
             "parity_spike_mismatches": mism, "clocks": clocks.summary()}
 
 
+def run_layernorm(args, dist, cfg):
+    """The pre-norm block's residual add + layer norm at the C5 chunk geometry:
+    h = x + delta, y = LayerNorm(h) over d (ops.add_layernorm, one pass)."""
+    from spikestack_lite_b200 import ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    d = cfg["d"]
+    R = (args.batch if args.batch is not None else cfg["batch"]) * cfg["rows_per_batch"]
+    g = torch.Generator(device=dev).manual_seed(21 + dist.rank)
+    x = torch.randn(R, d, generator=g, device=dev)
+    delta = torch.randn(R, d, generator=g, device=dev)
+    w = torch.randn(d, generator=g, device=dev)
+    b = torch.randn(d, generator=g, device=dev)
+
+    def step():
+        return ops.add_layernorm(x, delta, w, b, 1e-5)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if args.quick:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return {"workload": cfg["name"], "quick": True, "steps": args.steps}
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            h, y = step()
+        stop.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = dist.max(start.elapsed_time(stop)) / args.steps
+    ref = torch.nn.functional.layer_norm(x[:4096] + delta[:4096], (d,), w, b, 1e-5)
+    err = float((y[:4096] - ref).abs().max().item())
+    alg = 16.0 * R * d                            # x, delta read; h, y written
+    pk = peaks()
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(dist.world * gbs, 1), "unit": "GB/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "rows": R, "d": d,
+                       "l2": f"4 tensors of {R * d * 4 / 2**20:.0f} MiB > 126 MiB L2",
+                       "timing": "eager steps (one launch each), CUDA events, max over ranks"},
+            "roofline": {"kernel": "add_layernorm_kernel", "bound": "hbm", "achieved": round(gbs, 1),
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
+                         "alg_bytes_per_launch": int(alg), "traffic": None, "peak_src": pk["src"]},
+            "max_abs_err_vs_torch": err, "clocks": clocks.summary()}
+
+
 # ------------------------------------------------------------------- model
 def run_model(args, dist, cfg):
     from spikestack_lite_b200.transformer import SpikingTransformer
@@ -534,6 +588,8 @@ WORKLOADS = {
                "rows_per_batch": 4 * 1024, "K": 512, "N": 2048, "thr": 0.0},
     "attention": {"name": "spiking linear attention B=64 H=8 L=4096 dh=64 T=4 p=0.15", "T": 4, "B": 64,
                   "L": 4096, "H": 8, "dh": 64, "p": 0.15},
+    "layernorm": {"name": "block residual add + layer norm, C5 chunk: [4*64*1024, 512]", "batch": 64,
+                  "rows_per_batch": 4 * 1024, "d": 512},
     "model_small": {"name": "SpikingTransformer fwd, batch 256, seq 64, d 128, 1 layer, T=3", "batch": 256,
                     "model": dict(input_dim=48, d_model=128, seq_len=64, num_classes=10, num_heads=4, num_layers=1,
                                   n_repeats=3, temporal=True, expansion=4, use_spikeskip=True)},
@@ -591,6 +647,8 @@ def main():
             res = run_attention(args, dist, cfg)
         elif args.workload == "linear":
             res = run_linear(args, dist, cfg)
+        elif args.workload == "layernorm":
+            res = run_layernorm(args, dist, cfg)
         else:
             res = run_model(args, dist, cfg)
         if dist.rank == 0:

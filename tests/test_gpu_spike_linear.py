@@ -52,6 +52,31 @@ def test_bf16_weight_sweep_shape(branch):
     assert O.rel_err(Y.cpu().numpy(), ref) < TOL
 
 
+@pytest.mark.parametrize("T,M,K,N,p", [(2, 300, 512, 200, 0.2), (1, 130, 64, 65, 0.5), (3, 1000, 256, 128, 0.1)])
+def test_bf16_weight_partial_tiles_bias_csr(T, M, K, N, p):
+    # bf16 weights on the dense branch: partial N tile, bias, CSR outputs
+    S = _spikes(T, M, K, p, seed=M + 3)
+    W = _weight(N, K, seed=N + 3, dtype=torch.bfloat16)
+    b = torch.randn(N, device="cuda")
+    csr = ops.alloc_csr(T, M, K, "cuda")
+    Y = ops.spike_linear(S, weight=W, bias=b, csr=csr, branch="dense")
+    ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy()) + b.cpu().numpy()
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+    exp = O.csr_planes(S.cpu().numpy())
+    assert np.array_equal(csr["row_ptr"].cpu().numpy().reshape(-1), exp[1].reshape(-1))
+    assert np.array_equal(csr["col_idx"][: exp[2].size].cpu().numpy(), exp[2])
+
+
+def test_bf16_weight_real_valued_inputs():
+    # real-valued S with bf16 W: the converters split non-exact S values into hi + lo
+    g = torch.Generator(device="cuda").manual_seed(12)
+    S = torch.randn(2, 260, 512, generator=g, device="cuda")
+    W = _weight(192, 512, seed=13, dtype=torch.bfloat16)
+    Y = ops.spike_linear(S, weight=W, branch="dense")
+    ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy())
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+
+
 def test_csr_branch_bit_exact_with_reference_order():
     S = _spikes(2, 300, 512, 0.1, seed=4)
     W = _weight(128, 512, seed=5)
