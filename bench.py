@@ -553,9 +553,16 @@ def run_model(args, dist, cfg):
     x_all = torch.randn(B, cfg["model"]["seq_len"], cfg["model"]["input_dim"], generator=g)
     x = x_all[lo:hi].to(dev)  # this rank's samples, resident before timing
     chunk = min(cfg.get("chunk", hi - lo), hi - lo)
+    graphed = not args.eager and (hi - lo) % chunk == 0
+    if graphed:
+        from spikestack_lite_b200.graphs import CapturedForward
+
+        fwd_chunk = CapturedForward(model, x[:chunk])  # one graph per chunk shape, replayed for every chunk
+    else:
+        fwd_chunk = model
 
     def fwd():
-        local = torch.cat([model(x[i:i + chunk]) for i in range(0, hi - lo, chunk)])
+        local = torch.cat([fwd_chunk(x[i:i + chunk]).clone() for i in range(0, hi - lo, chunk)])
         return dist.gather_rows(local)  # NCCL all-gather of the logits: the only collective
 
     with torch.no_grad():
@@ -575,7 +582,10 @@ def run_model(args, dist, cfg):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg["name"], "global_batch": B, "seq_len": cfg["model"]["seq_len"],
-                       "parallelism": f"batch-sharded x{dist.world}, NCCL all_gather of logits"},
+                       "parallelism": f"batch-sharded x{dist.world}, NCCL all_gather of logits",
+                       "timing": (f"forward of each {chunk}-sample chunk replayed from one CUDA graph "
+                                  "(spikestack_lite_b200.graphs.CapturedForward)" if graphed else "eager forward")
+                       + ", CUDA events, max over ranks"},
             "logits_checksum": float(logits.double().sum().item())}
 
 
@@ -612,6 +622,7 @@ def main():
     ap.add_argument("--branch", default="dense", choices=["auto", "dense", "csr"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="eager steps only, no JSON metrics (profiling case)")
+    ap.add_argument("--eager", action="store_true", help="model workloads: eager forward instead of a CUDA graph")
     ap.add_argument("--rows", type=int, default=None, help="override M (rows per plane) of spike-linear workloads")
     ap.add_argument("--batch", type=int, default=None, help="override B of the attention workload")
     args = ap.parse_args()

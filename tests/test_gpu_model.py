@@ -45,3 +45,17 @@ def test_end_to_end_logits(golden, name):
     with torch.no_grad():
         logits = m(torch.from_numpy(z["x"]).cuda())
     assert O.rel_err(logits.cpu().numpy(), z["logits"]) < 5e-3
+
+
+def test_captured_forward_matches_eager(golden):
+    from spikestack_lite_b200.graphs import CapturedForward
+
+    z = golden("model_c1")
+    m, cfg = _model(z)
+    x = torch.from_numpy(z["x"]).cuda()
+    with torch.no_grad():
+        eager = m(x)
+        cap = CapturedForward(m, x)
+        assert torch.equal(cap(x), eager)
+        x2 = torch.randn_like(x)
+        assert torch.equal(cap(x2).clone(), m(x2))
