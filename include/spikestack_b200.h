@@ -223,6 +223,18 @@ int spk_gsmc_forward(const float* gi_all, const float* wd_all, const float* w_re
 int spk_add_layernorm(const float* X, const float* D, const float* gamma, const float* beta, int64_t rows, int d,
                       float eps, float* H, float* Y, spk_stream_t stream);
 
+/* ------------------------------------------------------- Spire planes
+ * The Spire encoder's temporal planes (SpireEncoder.forward, encode/spire.py:
+ * 60-69; spire_dither_kernel, encode/src/spire_cuda.cu:7-58) from the
+ * projection u [B, N, d]:
+ *   v = (u - frontier[c]) - temporal_frontier[n],
+ *   planes[t, b, n, c] = (v - dither[t] > 0) ? 1 : 0   for t < T,
+ * planes [T, B, N, d] contiguous.  frontier [d] and temporal_frontier [N] may be
+ * null (the term is then left out: spire_dither(v, dither) of the reference
+ * engine).  d % 4 == 0; u, planes and frontier 16-byte aligned. */
+int spk_spire_planes(const float* u, const float* frontier, const float* temporal_frontier, const float* dither,
+                     int T, int64_t B, int N, int d, float* planes, spk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,6 @@
 """Engine objects with the reference's pybind names.
 
-The reference loads three torch extensions and keeps them in module globals
+The reference loads four torch extensions and keeps them in module globals
 that its Python layer calls (and its tests monkeypatch):
 
     spikestack_lite.sparse._cuda_engine          sparse_forward, sparse_multistep_forward, dense_to_csr_gpu
@@ -8,6 +8,7 @@ that its Python layer calls (and its tests monkeypatch):
     spikestack_lite.nn.attention._attn_cuda_engine  apply_channel_decay, fused_normalize_attention
                                                  (attention_cuda.cu:109-112)
     spikestack_lite.nn.gsmc._gsmc_cuda_engine    fused_gsmc_step (gsmc_cuda.cu:129-132)
+    spikestack_lite.encode.spire._spire_cuda_engine  spire_dither (encode/src/spire_cuda.cu:60-62)
 
 The objects below answer to the same names and argument lists, backed by
 libspk_b200.so.  ``install(spikestack_lite)`` swaps them into an imported
@@ -52,6 +53,15 @@ class AttentionEngine:
         return ops.spiking_attention(q, k, v, lam, heads, eps)
 
 
+class SpireEngine:
+    """Replacement for ``encode.spire._spire_cuda_engine``."""
+
+    name = "spikestack_lite_b200.spire"
+
+    def spire_dither(self, v, dither):
+        return ops.spire_dither(v, dither)
+
+
 class GsmcEngine:
     """Replacement for ``nn.gsmc._gsmc_cuda_engine``."""
 
@@ -68,6 +78,7 @@ class GsmcEngine:
 sparse_engine = SparseEngine()
 attention_engine = AttentionEngine()
 gsmc_engine = GsmcEngine()
+spire_engine = SpireEngine()
 
 
 def install(reference_pkg):
@@ -82,4 +93,10 @@ def install(reference_pkg):
     sparse._cuda_engine = sparse_engine
     attn._attn_cuda_engine = attention_engine
     gsmc._gsmc_cuda_engine = gsmc_engine
+    try:
+        spire = importlib.import_module(reference_pkg.__name__ + ".encode.spire")
+    except ImportError:
+        spire = None
+    if spire is not None:
+        spire._spire_cuda_engine = spire_engine
     return reference_pkg

@@ -339,3 +339,38 @@ def add_layernorm(x, delta, weight=None, bias=None, eps=1e-5):
                                         ptr(h) if delta is not None else None, ptr(y), stream_of(x)),
           "spk_add_layernorm")
     return h, y
+
+
+# --------------------------------------------------------------------------- Spire planes
+def spire_planes(u, dither, frontier=None, temporal_frontier=None):
+    """The Spire encoder's temporal planes (encode/spire.py:60-69) in one pass
+    (spk_spire_planes): for u [B, N, d] and dither [T],
+    planes[t] = ((u - frontier) - temporal_frontier[n]) - dither[t] > 0 as
+    float32 [T, B, N, d]; frontier [d] and temporal_frontier [N] (any shape
+    with those element counts) may be None."""
+    require_cuda(u, dither, frontier, temporal_frontier, what="spire_planes")
+    require_f32(u, dither, frontier, temporal_frontier, what="spire_planes")
+    if u.dim() != 3:
+        raise EngineError("spire_planes: u must be (B, N, d)")
+    B, N, d = u.shape
+    u = _contig(u)
+    dither = _contig(dither).view(-1)
+    if frontier is not None:
+        frontier = _contig(frontier).view(-1)
+        if frontier.numel() != d:
+            raise EngineError(f"spire_planes: frontier must have d={d} elements")
+    if temporal_frontier is not None:
+        temporal_frontier = _contig(temporal_frontier).view(-1)
+        if temporal_frontier.numel() != N:
+            raise EngineError(f"spire_planes: temporal_frontier must have N={N} elements")
+    T = dither.numel()
+    planes = torch.empty(T, B, N, d, dtype=torch.float32, device=u.device)
+    check(_lib.load().spk_spire_planes(ptr(u), ptr(frontier), ptr(temporal_frontier), ptr(dither), T, B, N, d,
+                                       ptr(planes), stream_of(u)), "spk_spire_planes")
+    return planes
+
+
+def spire_dither(v, dither):
+    """spire_dither(v [B, N, d], dither [T]) -> (v - dither[t] > 0) as float32
+    [T, B, N, d]: the reference Spire engine's entry point (spire_cuda.cu:28-58)."""
+    return spire_planes(v, dither)

@@ -17,6 +17,7 @@ use them.
 import torch
 import torch.nn as nn
 
+from . import ops
 from ._lib import EngineError
 from .attention import AstrocyteHebbianBlock, spike_fn
 from .gsmc import FusedGSMC
@@ -38,13 +39,15 @@ class SpireEncoder(nn.Module):
 
     def forward(self, x):
         u = self.projection(x)
+        if (self.temporal and not torch.is_grad_enabled() and u.is_cuda and u.dtype == torch.float32
+                and self.d_model % 4 == 0):
+            # inference: the planes in one engine pass from u, (R, B, N, d)
+            # contiguous as the reference engine's spire_dither returns them
+            return ops.spire_planes(u, self.dither.float(), self.frontier, self.temporal_frontier)
         v = (u - self.frontier.view(1, 1, self.d_model) - self.temporal_frontier).float()
         if self.n_repeats == 1 and not self.temporal:
             return spike_fn(v)
         if self.temporal:
-            # the planes (R, B, N, d) laid out contiguously: the reference's
-            # permute of the (B, N, d, R) comparison has the same values but
-            # leaves every later residual add and layer norm on a strided view
             return spike_fn(v.unsqueeze(0) - self.dither.float().view(-1, 1, 1, 1))
         return spike_fn(v.unsqueeze(-1) - self.dither.float()).permute(3, 0, 1, 2).mean(dim=0)
 

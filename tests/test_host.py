@@ -112,7 +112,7 @@ def test_alloc_csr_buffers_shapes():
 def test_install_swaps_engines_into_a_reference_package():
     pkg = types.ModuleType("fakeref")
     mods = {n: types.ModuleType(n) for n in ("fakeref.sparse", "fakeref.nn", "fakeref.nn.attention",
-                                             "fakeref.nn.gsmc")}
+                                             "fakeref.nn.gsmc", "fakeref.encode", "fakeref.encode.spire")}
     import sys
 
     sys.modules["fakeref"] = pkg
@@ -122,6 +122,7 @@ def test_install_swaps_engines_into_a_reference_package():
         assert mods["fakeref.sparse"]._cuda_engine is E.sparse_engine
         assert mods["fakeref.nn.attention"]._attn_cuda_engine is E.attention_engine
         assert mods["fakeref.nn.gsmc"]._gsmc_cuda_engine is E.gsmc_engine
+        assert mods["fakeref.encode.spire"]._spire_cuda_engine is E.spire_engine
     finally:
         for n in ["fakeref", *mods]:
             sys.modules.pop(n, None)
@@ -133,3 +134,4 @@ def test_engine_objects_expose_reference_names():
     for name in ("apply_channel_decay", "fused_normalize_attention"):
         assert callable(getattr(E.attention_engine, name))
     assert callable(E.gsmc_engine.fused_gsmc_step)
+    assert callable(E.spire_engine.spire_dither)
