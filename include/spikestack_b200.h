@@ -235,6 +235,16 @@ int spk_add_layernorm(const float* X, const float* D, const float* gamma, const 
 int spk_spire_planes(const float* u, const float* frontier, const float* temporal_frontier, const float* dither,
                      int T, int64_t B, int N, int d, float* planes, spk_stream_t stream);
 
+/* ------------------------------------------------------- readout pooling
+ * The pooling before SpikingTransformer's classifier (models/transformer.py:
+ * 159-192): over x [T, B, N, d] (T = 1 for the GSMC-pooled [B, N, d]), per
+ * sample b and channel c, mean_x[b, c] = mean over (t, n) of x and
+ * mean_spike[b, c] = mean over (t, n) of (x > 0), each (sum) * (1 / (T N)) as
+ * torch's mean; either output may be null.  d % 4 == 0, T*N < 2^24, tensors
+ * 16-byte aligned. */
+int spk_temporal_mean(const float* x, int T, int64_t B, int N, int d, float* mean_x, float* mean_spike,
+                      spk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

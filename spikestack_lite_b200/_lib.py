@@ -49,6 +49,7 @@ SIGNATURES = {
     "spk_gsmc_forward": (_I, [_P, _P, _P, _P, _I, _L, _I, _F, _F, _I, _F, _I, _P, _P, _P, _Z, _P]),
     "spk_add_layernorm": (_I, [_P, _P, _P, _P, _L, _I, _F, _P, _P, _P]),
     "spk_spire_planes": (_I, [_P, _P, _P, _P, _I, _L, _I, _I, _P, _P]),
+    "spk_temporal_mean": (_I, [_P, _I, _L, _I, _I, _P, _P, _P]),
 }
 
 _lib = None

@@ -374,3 +374,25 @@ def spire_dither(v, dither):
     """spire_dither(v [B, N, d], dither [T]) -> (v - dither[t] > 0) as float32
     [T, B, N, d]: the reference Spire engine's entry point (spire_cuda.cu:28-58)."""
     return spire_planes(v, dither)
+
+
+# --------------------------------------------------------------------------- readout pooling
+def temporal_mean(x):
+    """(mean of x, mean of (x > 0)) over (t, n) per sample and channel for a
+    temporal context x [T, B, N, d], or over n for [B, N, d] (the pooling in
+    front of SpikingTransformer's classifier, models/transformer.py:159-192),
+    in one pass (spk_temporal_mean).  Both results [B, d] float32."""
+    require_cuda(x, what="temporal_mean")
+    require_f32(x, what="temporal_mean")
+    if x.dim() == 3:
+        T, (B, N, d) = 1, x.shape
+    elif x.dim() == 4:
+        T, B, N, d = x.shape
+    else:
+        raise EngineError("temporal_mean: x must be (T, B, N, d) or (B, N, d)")
+    x = _contig(x)
+    mean_x = torch.empty(B, d, dtype=torch.float32, device=x.device)
+    mean_s = torch.empty(B, d, dtype=torch.float32, device=x.device)
+    check(_lib.load().spk_temporal_mean(ptr(x), T, B, N, d, ptr(mean_x), ptr(mean_s), stream_of(x)),
+          "spk_temporal_mean")
+    return mean_x, mean_s

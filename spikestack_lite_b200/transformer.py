@@ -131,6 +131,11 @@ class SpikingTransformer(nn.Module):
             context, context_norm = block.forward_fused(context, context_norm, nxt)
         if self.gsmc is not None:
             context = self.gsmc(context, T=context.shape[0])
-        self._pooled_for_latency = context.mean(dim=(0, 2)) if (self.temporal and self.gsmc is None) \
-            else context.mean(dim=1)
+        pooled_over_time = self.temporal and self.gsmc is None
+        if (self.spike_readout and not torch.is_grad_enabled() and context.dtype == torch.float32
+                and context.dim() == (4 if pooled_over_time else 3) and context.shape[-1] % 4 == 0):
+            # inference: both poolings (the latency head's and the classifier's) in one pass
+            self._pooled_for_latency, pooled_spikes = ops.temporal_mean(context)
+            return self.classifier(pooled_spikes)
+        self._pooled_for_latency = context.mean(dim=(0, 2)) if pooled_over_time else context.mean(dim=1)
         return self.readout(context)
