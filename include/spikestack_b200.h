@@ -69,6 +69,11 @@ int spk_device_error(int clear, int* out_bits);
  * block << 40 | warp << 32 | shared-memory address of the mbarrier (0 when no
  * wait timed out).  Synchronizes the device. */
 int spk_timeout_site(uint64_t* out_site);
+/* Self-test of the failure detection: launches one thread that waits on an
+ * mbarrier nothing completes; after the wait's bound (2 s) the kernel records
+ * SPK_DEV_PIPE_TIMEOUT and its site (spk_device_error, spk_timeout_site) and
+ * exits, leaving the context usable.  No reference counterpart. */
+int spk_selftest_wait_timeout(spk_stream_t stream);
 /* Number of this library's kernel launches issued so far from this process
  * (all threads, all devices).  Used to report gpu_launches. */
 int64_t spk_launch_count(void);

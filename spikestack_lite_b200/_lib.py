@@ -15,6 +15,8 @@ LIB_PATH = os.path.join(HERE, "libspk_b200.so")
 
 SPK_OK, SPK_EINVAL, SPK_EUNSUPPORTED, SPK_ECUDA, SPK_EWORKSPACE, SPK_EDEVICE = range(6)
 SPK_F32, SPK_BF16 = 0, 1
+# device error bits (spk_device_error)
+SPK_DEV_PIPE_TIMEOUT, SPK_DEV_SCAN_TIMEOUT, SPK_DEV_CSR_OVERFLOW, SPK_DEV_TMEM = 1, 2, 4, 8
 BRANCH_AUTO, BRANCH_DENSE, BRANCH_CSR = 0, 1, 2
 BRANCHES = {"auto": BRANCH_AUTO, "dense": BRANCH_DENSE, "csr": BRANCH_CSR}
 
@@ -48,6 +50,7 @@ SIGNATURES = {
     "spk_gsmc_workspace_bytes": (_Z, [_L, _I]),
     "spk_gsmc_forward": (_I, [_P, _P, _P, _P, _I, _L, _I, _F, _F, _I, _F, _I, _P, _P, _P, _Z, _P]),
     "spk_add_layernorm": (_I, [_P, _P, _P, _P, _L, _I, _F, _P, _P, _P]),
+    "spk_selftest_wait_timeout": (_I, [_P]),
     "spk_spire_planes": (_I, [_P, _P, _P, _P, _I, _L, _I, _I, _P, _P]),
     "spk_temporal_mean": (_I, [_P, _I, _L, _I, _I, _P, _P, _P]),
 }
