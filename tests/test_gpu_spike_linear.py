@@ -42,6 +42,35 @@ def test_spike_linear_vs_oracle(branch, T, M, K, N, p):
     assert O.rel_err(Y.cpu().numpy(), ref) < TOL
 
 
+@pytest.mark.parametrize("T,M,K,N,p", [
+    (3, 16384, 512, 128, 0.10),   # the isolated spike-linear config
+    (2, 300, 96, 200, 0.3),       # K not a multiple of 64, partial N tile, partial row tile
+    (1, 1000, 2048, 512, 0.5),    # four N tiles
+])
+def test_weightT_layout_dense_branch(T, M, K, N, p):
+    # weightT [K, N] contiguous (the reference ops' layout) on the dense branch:
+    # the same results as the nn.Linear layout, CSR outputs included
+    S = _spikes(T, M, K, p, seed=M + 7)
+    WT = _weight(N, K, seed=N + 7).t().contiguous()
+    b = torch.randn(N, device="cuda")
+    csr = ops.alloc_csr(T, M, K, "cuda")
+    Y = ops.spike_linear(S, weightT=WT, bias=b, csr=csr, branch="dense")
+    ref = O.spike_linear(S.cpu().numpy(), WT.cpu().numpy()) + b.cpu().numpy()
+    assert O.rel_err(Y.cpu().numpy(), ref) < TOL
+    assert torch.equal(Y, ops.spike_linear(S, weight=WT.t(), bias=b, branch="dense"))
+    exp = O.csr_planes(S.cpu().numpy())
+    assert np.array_equal(csr["row_ptr"].cpu().numpy().reshape(-1), exp[1].reshape(-1))
+    assert np.array_equal(csr["col_idx"][: exp[2].size].cpu().numpy(), exp[2])
+
+
+def test_weightT_layout_real_valued_inputs():
+    g = torch.Generator(device="cuda").manual_seed(31)
+    S = torch.randn(2, 260, 512, generator=g, device="cuda")
+    WT = _weight(192, 512, seed=32).t().contiguous()
+    Y = ops.spike_linear(S, weightT=WT, branch="dense")
+    assert O.rel_err(Y.cpu().numpy(), O.spike_linear(S.cpu().numpy(), WT.cpu().numpy())) < TOL
+
+
 @pytest.mark.parametrize("branch", ["dense", "csr"])
 def test_bf16_weight_sweep_shape(branch):
     # the density-sweep geometry (K = N = 2048, bf16 W, fp32 accumulate), row slice
