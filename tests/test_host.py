@@ -94,6 +94,28 @@ def test_add_layernorm_host_checks():
         blk.forward_fused(x, None, blk.norm1)
 
 
+def test_spire_and_readout_ops_host_checks():
+    from spikestack_lite_b200 import ops
+    from spikestack_lite_b200.graphs import CapturedForward
+    from spikestack_lite_b200.transformer import SpireEncoder
+
+    with pytest.raises(EngineError, match="CUDA"):
+        ops.spire_planes(torch.randn(2, 4, 8), torch.zeros(3))
+    with pytest.raises(EngineError, match="CUDA"):
+        ops.temporal_mean(torch.randn(3, 2, 4, 8))
+    with pytest.raises(EngineError, match="CUDA"):
+        CapturedForward(torch.nn.Identity(), torch.randn(2, 3))
+    # off the engine path (CPU, or autograd on) the encoder runs the reference's composition
+    torch.manual_seed(0)
+    enc = SpireEncoder(input_dim=6, d_model=8, seq_len=5, n_repeats=3, temporal=True)
+    x = torch.randn(2, 5, 6)
+    planes = enc(x)
+    u = enc.projection(x)
+    v = u - enc.frontier.view(1, 1, 8) - enc.temporal_frontier
+    want = (v.unsqueeze(-1) - enc.dither > 0).float().permute(3, 0, 1, 2)
+    assert planes.shape == (3, 2, 5, 8) and torch.equal(planes, want)
+
+
 def test_unsupported_stems_are_rejected():
     with pytest.raises(EngineError):
         SpikingTransformer(use_conv_stem=True)
