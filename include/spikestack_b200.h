@@ -34,7 +34,7 @@ typedef struct CUstream_st* spk_stream_t; /* identical to cudaStream_t */
 enum {
   SPK_OK = 0,
   SPK_EINVAL = 1,        /* bad argument (shape, pointer, alignment, dtype) */
-  SPK_EUNSUPPORTED = 2,  /* valid request this build does not implement */
+  SPK_EUNSUPPORTED = 2,  /* valid request the library does not implement */
   SPK_ECUDA = 3,         /* CUDA runtime error (launch or attribute) */
   SPK_EWORKSPACE = 4,    /* workspace missing or too small */
   SPK_EDEVICE = 5        /* a kernel reported a device-side error (spk_device_error) */

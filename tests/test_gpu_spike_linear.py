@@ -1,6 +1,6 @@
 """Spike-linear on the GPU against the oracle.
 
-Tolerance (north star): fp32 outputs within max-abs 1e-4 x max|ref|.  The CSR
+Tolerance: fp32 outputs within max-abs 1e-4 x max|ref|.  The CSR
 branch keeps the reference engine's summation order and is checked bit-exact
 (against the C restatement of csr_coalesced_kernel and against the reference
 engine itself); CSR indices and counts are always bit-exact."""
