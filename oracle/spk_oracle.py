@@ -341,7 +341,7 @@ def state_dict_from_golden(z):
 
 
 def rel_err(a, b):
-    """max |a - b| / max |b| (the north-star tolerance metric)."""
+    """max |a - b| / max |b| (the parity tolerance metric: fp32 outputs within 1e-4 of it)."""
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     scale = max(float(np.abs(b).max()) if b.size else 0.0, 1e-30)
