@@ -118,11 +118,13 @@ int spk_csr_compact(const float* S, int T, int64_t M, int K, int32_t* nnz_row, i
  * that own all device memory and give plugins no workspace, or serving loops
  * that forbid cudaMalloc after start-up): no workspace argument, the scan's
  * scratch lives in a fixed 1 MiB array inside the library, held by every GPU
- * that loads it.  No counterpart in the reference.  Limit: the scan needs
- * 256 bytes + 9 bytes per row tile (up to 128 rows of one plane), about
- * 116 000 tiles; larger requests return SPK_EWORKSPACE.  The first call on a
- * device looks the array's device address up (cudaGetSymbolAddress) and
- * should come before any stream capture on that device.  All calls share the
+ * that loads it.  No counterpart in the reference.  Limit: a problem fits
+ * when spk_csr_workspace_bytes(T, M, K) <= 1 MiB (256 bytes of state + 9
+ * bytes per row tile of up to 128 rows of one plane + 8 bytes per plane,
+ * rounded up to 256: about 116 000 tiles with few planes); larger requests
+ * return SPK_EWORKSPACE.  The first call on a device (and the first after its
+ * context was reset) looks the array's device address up
+ * (cudaGetSymbolAddress) and should come before any stream capture there.  All calls share the
  * array: calls that overlap on the GPU race, so issue them on one stream. */
 int spk_csr_compact_noalloc(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
                             int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity,

@@ -1,7 +1,8 @@
 """Build the reference's own CUDA engines from its sources, as a second checker.
 
-Compiles, from a checkout of Griffith-7/spikestack-lite (default
-/root/reference, read-only), the three engines on the hot path
+Compiles, from a checkout of Griffith-7/spikestack-lite (``--reference PATH``
+or the SPIKESTACK_REFERENCE environment variable; read-only), the three
+engines on the hot path
 
     spikestack_lite/sparse/src/sparse_linear.cu   -> oracle/_ref/spikeskip_ref/
     spikestack_lite/nn/src/attention_cuda.cu      -> oracle/_ref/attention_ref/
@@ -28,8 +29,14 @@ ENGINES = {
 }
 
 
-def build_ref(reference="/root/reference", verbose=False):
+def build_ref(reference=None, verbose=False):
+    """Compile the reference engines from the checkout at ``reference`` (or the
+    directory named by the SPIKESTACK_REFERENCE environment variable)."""
     from torch.utils.cpp_extension import load
+
+    reference = reference or os.environ.get("SPIKESTACK_REFERENCE")
+    if not reference:
+        raise RuntimeError("no reference checkout given: pass --reference PATH or set SPIKESTACK_REFERENCE")
 
     built = {}
     for name, rel in ENGINES.items():
@@ -62,7 +69,10 @@ def load_ref(name):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SPIKESTACK_REFERENCE"),
+                    help="reference checkout (default: $SPIKESTACK_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference PATH or set SPIKESTACK_REFERENCE")
     print(build_ref(a.reference, verbose=True))
     sys.exit(0)

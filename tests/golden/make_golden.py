@@ -2,7 +2,7 @@
 
 These fixtures are produced by the REFERENCE implementation itself (its own
 PyTorch CPU code paths), imported from a local checkout given by
-``--reference`` (default: ``/root/reference``).  They exist so that the oracle
+``--reference`` (default: the SPIKESTACK_REFERENCE environment variable).  They exist so that the oracle
 restatement in ``oracle/`` can be pinned against the reference on machines
 where the reference is not available (the GPU box has no checkout).
 
@@ -173,9 +173,12 @@ def make_models(out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SPIKESTACK_REFERENCE"),
+                    help="reference checkout (default: $SPIKESTACK_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference PATH or set SPIKESTACK_REFERENCE")
     sys.path.insert(0, a.reference)
     torch.set_num_threads(1)
     make_spike_linear(a.out)

@@ -80,7 +80,13 @@ def test_noalloc_rejects_problems_beyond_the_fixed_scratch(lib):
     one = torch.zeros(64, dtype=torch.int32, device=dev)
     pp = torch.zeros(2, dtype=torch.int64, device=dev)
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    # 64 planes x 2^18 rows of 64 columns = 131072 row tiles: above the 1 MiB array
+    # 64 planes x 2^18 rows of 64 columns = 131072 row tiles: above the 1 MiB array.
+    # The buffers below are tiny, so only the size check may stop this call:
+    # confirm on the host that the shape is over the limit before calling, so a
+    # regressed limit fails here instead of launching on undersized buffers.
+    need = lib.spk_csr_workspace_bytes(64, 1 << 18, 64)
+    if need <= 1 << 20:
+        pytest.fail(f"the rejection shape needs only {need} bytes of scratch; it no longer exceeds the 1 MiB array")
     rc = lib.spk_csr_compact_noalloc(_ptr(S), 64, 1 << 18, 64, None, _ptr(one), _ptr(one), None, _ptr(pp), 64,
                                      stream)
     assert rc == SPK_EWORKSPACE
