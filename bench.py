@@ -1,22 +1,25 @@
 #!/usr/bin/env python
 """Benchmark of the SpikeStack Lite hot path on B200.
 
-Default workload (one "step"): the isolated spike-linear configuration --
-binary spikes S[T=3, M=16384, K=512] ~ Bernoulli(0.10) per plane, W[K=512,
-N=128] fp32 ~ N(0, 1/K), output Y fp32 [T, M, N], CSR built per plane --
-through the engine's spike-linear (dense tcgen05 branch + per-plane CSR).
-Metric: GSOP/s, SOP = one (nonzero input spike, output neuron) accumulate,
-SOPs per step = nnz(S) * N.
+Default workload (one "step"): the full SpikingTransformer forward at batch
+512, seq 1024, input 256, d 512, 8 heads, 6 layers, T = 4 Spire planes, FFN
+x4, GSMC on (x ~ N(0, 1), random-init weights from torch.manual_seed(0)),
+batch-sharded over the N GPUs: each rank runs its 512/N samples in chunks of
+64 (each chunk's forward replayed from one CUDA graph) and one NCCL
+all_gather of the logits rebuilds the batch inside the timed region.  Metric:
+tokens/s = 512 * 1024 / step time (strong scaling: the batch is fixed).
+The line nests the isolated spike-linear measurement under "spike_linear":
+S[T=3, M=16384, K=512] ~ Bernoulli(0.10), W[512, 128] fp32, Y fp32, CSR per
+plane, in GSOP/s (SOP = one nonzero input spike x one output neuron) with its
+HBM roofline (each rank its own instance, weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spike_linear|sweep|attention|linear|layernorm|model_small|model_full]
+                    [--workload model_full|spike_linear|sweep|attention|linear|layernorm|model_small]
 
-N > 1: launched by torchrun, one rank per GPU; every rank runs its own
-instance (the rows are independent -> weak scaling, no collective on the data
-path); value = all ranks' SOPs / max-over-ranks device time.
---impl reference: the reference's own CPU implementation of the path (its
-torch.matmul fallback, restated in oracle/) timed on the host cores, rank 0
-only.
+N > 1: launched by torchrun, one rank per GPU, timing on the device with CUDA
+events, max over ranks.  --impl reference: the reference's own CPU
+implementation of the path (its PyTorch CPU arithmetic, restated in oracle/)
+timed on all host cores, rank 0 only, on a sample of the same workload.
 """
 import argparse
 import json
@@ -27,8 +30,18 @@ import sys
 import threading
 import time
 
-import numpy as np
-import torch
+# The reference arm times the CPU path with every host core.  torchrun exports
+# OMP_NUM_THREADS=1 to each rank; set the pools' sizes before torch starts them.
+if "reference" in sys.argv:
+    try:
+        _n = str(len(os.sched_getaffinity(0)))
+    except AttributeError:
+        _n = str(os.cpu_count() or 1)
+    for _v in ("OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = _n
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -49,6 +62,14 @@ def peaks():
                 "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "src": "measured"}
     except Exception:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def host_threads():
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def profile_traffic(name):
@@ -327,7 +348,7 @@ def cpu_baseline_spike_linear(cfg, S_dev, W, budget_s=10.0):
     restated in oracle/) on a bounded sample, all host threads."""
     from oracle import spk_oracle as O
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(host_threads())
     S = S_dev.cpu()
     Wc = W.float().cpu()
     nnz = float((S > 0).sum().item())
@@ -348,7 +369,7 @@ def run_reference_spike_linear(args, dist, cfg):
     """--impl reference: the reference's CPU implementation, rank 0 only."""
     from oracle import spk_oracle as O
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(host_threads())
     g = torch.Generator().manual_seed(1234)
     T, M, K, N = cfg["T"], cfg["M"], cfg["K"], cfg["N"]
     W = torch.randn(K, N, generator=g) / K ** 0.5
@@ -544,55 +565,262 @@ def run_layernorm(args, dist, cfg):
 
 
 # ------------------------------------------------------------------- model
-def run_model(args, dist, cfg):
+def model_config(cfg, world):
+    """The model line's `config` (identical for both arms)."""
+    mc = cfg["model"]
+    return {"workload": cfg["name"], "global_batch": cfg["batch"], "seq_len": mc["seq_len"],
+            "input_dim": mc["input_dim"], "d_model": mc["d_model"], "layers": mc["num_layers"],
+            "heads": mc["num_heads"], "T": mc["n_repeats"], "gsmc": bool(mc.get("use_gsmc", False)),
+            "parallelism": f"batch-sharded over {world} GPU(s), NCCL all_gather of the logits",
+            "l2": "inputs larger than L2: every chunk's activations are >= 1 GiB (126 MiB L2)"}
+
+
+def model_inputs(cfg):
+    """x ~ N(0, 1) fp32 [batch, seq, input_dim], seeded (host tensor)."""
+    mc = cfg["model"]
+    g = torch.Generator().manual_seed(1)
+    return torch.randn(cfg["batch"], mc["seq_len"], mc["input_dim"], generator=g)
+
+
+def build_model(cfg, dev):
+    """Random-init weights from torch.manual_seed(0), as the reference builds the model."""
     from spikestack_lite_b200.transformer import SpikingTransformer
+
+    torch.manual_seed(0)
+    return SpikingTransformer(**cfg["model"]).to(dev).eval()
+
+
+def model_cpu_sample(cfg, sd, x, n):
+    """The reference's CPU forward (restated in oracle/: the reference's own
+    PyTorch CPU arithmetic, pinned to its golden models) on the first n samples."""
+    from oracle import spk_oracle as O
+
+    mc = cfg["model"]
+    return O.transformer_forward(sd, x[:n], mc["num_heads"], mc["num_layers"], use_gsmc=mc.get("use_gsmc", False),
+                                 spike_readout=True, threshold=mc.get("spike_threshold", 0.0))
+
+
+def time_cpu_model(cfg, sd, x, n, budget_s=None, steps=None, warmup=1):
+    """Seconds per call of model_cpu_sample over n samples: median within a time
+    budget, or the mean of `steps` calls after `warmup`."""
+    torch.set_num_threads(host_threads())
+    for _ in range(warmup):
+        model_cpu_sample(cfg, sd, x, n)
+    times = []
+    if steps is not None:
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            model_cpu_sample(cfg, sd, x, n)
+        return (time.perf_counter() - t0) / steps, steps
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        model_cpu_sample(cfg, sd, x, n)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def model_kernel_profile(model, xc):
+    """One eager chunk forward with the engine's per-class launch timing (CUDA
+    events on the launch stream) and the tally of its contractions."""
+    from spikestack_lite_b200 import _lib, ops
+
+    prof = {}
+    for kname in ("dense", "attn_kv", "attn_out", "gsmc_step", "w_image"):
+        _lib.profile_begin(kname)
+        with ops.tally() as tl:
+            model(xc)
+        tot, n = _lib.profile_end()
+        prof[kname] = (tot, n)
+    torch.cuda.synchronize()
+    return prof, tl
+
+
+def run_model(args, dist, cfg):
+    from spikestack_lite_b200 import _lib
+    from spikestack_lite_b200.graphs import CapturedForward
 
     dev = torch.device("cuda", dist.local)
     torch.cuda.set_device(dev)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
-    torch.manual_seed(0)
-    model = SpikingTransformer(**cfg["model"]).to(dev).eval()
+    model = build_model(cfg, dev)
+    mc = cfg["model"]
     B = cfg["batch"]
     lo, hi = shard_bounds(B, dist.rank, dist.world)
-    g = torch.Generator().manual_seed(1)
-    x_all = torch.randn(B, cfg["model"]["seq_len"], cfg["model"]["input_dim"], generator=g)
-    x = x_all[lo:hi].to(dev)  # this rank's samples, resident before timing
+    x_all = model_inputs(cfg)
+    x = x_all[lo:hi].to(dev)  # this rank's samples, resident before the timed region
     chunk = min(cfg.get("chunk", hi - lo), hi - lo)
-    graphed = not args.eager and (hi - lo) % chunk == 0
-    if graphed:
-        from spikestack_lite_b200.graphs import CapturedForward
-
+    if (hi - lo) % chunk:
+        raise SystemExit(f"{hi - lo} samples per rank do not split into chunks of {chunk}")
+    n_chunks = (hi - lo) // chunk
+    launches0 = _lib.launch_count()
+    with torch.no_grad():
         fwd_chunk = CapturedForward(model, x[:chunk])  # one graph per chunk shape, replayed for every chunk
-    else:
-        fwd_chunk = model
+    launches_per_chunk = (_lib.launch_count() - launches0) // 2  # the eager warm-up call, then the capture
 
-    def fwd():
-        local = torch.cat([fwd_chunk(x[i:i + chunk]).clone() for i in range(0, hi - lo, chunk)])
-        return dist.gather_rows(local)  # NCCL all-gather of the logits: the only collective
+    def fwd(xs):
+        local = torch.cat([fwd_chunk(xs[i * chunk:(i + 1) * chunk]).clone() for i in range(n_chunks)])
+        return dist.gather_rows(local)  # NCCL all_gather of the logits: the only collective
 
+    stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(args.warmup):
-            fwd()
+            fwd(x)
         torch.cuda.synchronize()
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.barrier()
-        start.record()
-        for _ in range(args.steps):
-            logits = fwd()
-        stop.record()
+        with ClockSampler(dev.index) as clocks:
+            dist.barrier()
+            torch.cuda.synchronize()
+            start.record(stream)
+            for _ in range(args.steps):
+                logits = fwd(x)
+            stop.record(stream)
+            torch.cuda.synchronize()
+            dist.barrier()
+        ms = dist.max(start.elapsed_time(stop)) / args.steps
+        prof, tl = model_kernel_profile(model, x[:chunk])
+        e2e = model_e2e(args, dist, fwd_chunk, x_all[lo:hi], chunk, n_chunks, mc["num_classes"])
+    tokens = B * mc["seq_len"]
+    res = {"metric": METRIC, "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": dist.world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic: x ~ N(0,1) seeded, random-init weights from torch.manual_seed(0)",
+           "config": model_config(cfg, dist.world),
+           "timing": (f"forward of each {chunk}-sample chunk replayed from one CUDA graph "
+                      "(spikestack_lite_b200.graphs.CapturedForward), logits all_gather inside the region, "
+                      "CUDA events, max over ranks"),
+           "gpu_launches": int(launches_per_chunk * n_chunks * args.steps),
+           "clocks": clocks.summary(), "e2e": e2e}
+    res.update(model_roofline(prof, tl, mc))
+    res["logits_checksum"] = float(logits.double().sum().item())
+    if dist.rank == 0:
+        sd = {k: v.detach().cpu() for k, v in model.state_dict().items()}
+        n_par = 2
+        with torch.no_grad():
+            got = fwd_chunk(x[:chunk])[:n_par].cpu().numpy()
+        from oracle import spk_oracle as O
+
+        ref = model_cpu_sample(cfg, sd, x_all, n_par).numpy()
+        res["parity"] = {"logits_rel_err": O.rel_err(got, ref), "samples": n_par,
+                         "vs": "oracle CPU forward (the reference's arithmetic) on the same weights and inputs"}
+        if dist.world == 1 and not args.no_cpu_baseline:
+            n_cpu = 2
+            t, runs = time_cpu_model(cfg, sd, x_all, n_cpu, budget_s=12.0)
+            res["cpu_baseline"] = {"value": round(n_cpu * mc["seq_len"] / t, 1), "unit": "tokens/s",
+                                   "cores": torch.get_num_threads(), "kind": "port",
+                                   "sample": f"{n_cpu} of {B} samples per forward (samples are independent), "
+                                             f"median of {runs} runs",
+                                   "ms_per_sample_forward": round(t * 1e3 / n_cpu, 1)}
+    return res
+
+
+def model_e2e(args, dist, fwd_chunk, x_host, chunk, n_chunks, n_classes):
+    """The same metric through the public forward (CapturedForward / the
+    model's __call__) from pinned host inputs: every step copies each chunk of
+    this rank's samples host->device (a copy stream, two buffers, so chunk
+    i+1 crosses PCIe while chunk i computes), gathers the logits over NCCL and
+    reads them back to the host on rank 0."""
+    dev = torch.device("cuda", dist.local)
+    pinned = x_host.contiguous().pin_memory()
+    dbuf = [torch.empty((chunk,) + tuple(pinned.shape[1:]), device=dev) for _ in range(2)]
+    s_copy = torch.cuda.Stream(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_used:
+        e.record(stream)
+    host_logits = torch.empty((n_chunks * chunk * dist.world, n_classes)).pin_memory()
+
+    def step():
+        s_copy.wait_stream(stream)
+        outs = []
+        for i in range(n_chunks):
+            b = i % 2
+            with torch.cuda.stream(s_copy):
+                s_copy.wait_event(ev_used[b])
+                dbuf[b].copy_(pinned[i * chunk:(i + 1) * chunk], non_blocking=True)
+                ev_in[b].record(s_copy)
+            stream.wait_event(ev_in[b])
+            outs.append(fwd_chunk(dbuf[b]).clone())
+            ev_used[b].record(stream)
+        logits = dist.gather_rows(torch.cat(outs))
+        if dist.rank == 0:
+            host_logits.copy_(logits, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(2):
+            step()
         torch.cuda.synchronize()
-    ms = dist.max(start.elapsed_time(stop)) / args.steps
-    tokens = B * cfg["model"]["seq_len"]
-    return {"metric": METRIC, "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": dist.world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg["name"], "global_batch": B, "seq_len": cfg["model"]["seq_len"],
-                       "parallelism": f"batch-sharded x{dist.world}, NCCL all_gather of logits",
-                       "timing": (f"forward of each {chunk}-sample chunk replayed from one CUDA graph "
-                                  "(spikestack_lite_b200.graphs.CapturedForward)" if graphed else "eager forward")
-                       + ", CUDA events, max over ranks"},
-            "logits_checksum": float(logits.double().sum().item())}
+        steps = max(3, args.steps // 2)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = dist.max(start.elapsed_time(stop)) / steps
+    tokens = n_chunks * chunk * dist.world * pinned.shape[1]
+    return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": int(pinned.numel() * 4 * dist.world),
+            "d2h_bytes_per_step": int(host_logits.numel() * 4), "ms_per_step": round(ms, 3), "steps": steps,
+            "api": "spikestack_lite_b200.graphs.CapturedForward over SpikingTransformer (pinned host x in, "
+                   "logits out)", "copies": "all ranks' inputs H2D (whole job), gathered logits D2H on rank 0"}
+
+
+def model_roofline(prof, tl, mc):
+    """Roofline of the dominant kernel class: the tcgen05 contractions
+    (spike_linear_wt_kernel instances: the fp32-accurate linear op and the
+    spike-linear), tensor-bound at this geometry."""
+    pk = peaks()
+    tot, n = prof["dense"]
+    flops = tl.flops()  # algorithmic: 2*rows*K*N of every contraction in one chunk forward
+    passes = sum((3.0 if op == "linear_act" else 2.0) * 2.0 * r * k * nn for op, r, k, nn in tl.calls)
+    peak = pk["bf16_tflops_sustained"] / 2.0
+    ach = flops / (tot / 1e3) / 1e12 if tot else None
+    other = {k: round(v[0], 3) for k, v in prof.items()}
+    return {
+        "roofline": {"kernel": "spike_linear_wt_kernel (linear-op and spike-linear instances)", "bound": "tensor",
+                     "achieved": round(ach, 1) if ach else None, "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(ach / peak, 4) if ach else None,
+                     "alg_flops_per_launch": round(flops / max(n, 1)), "launches_per_chunk": n,
+                     "traffic": None,
+                     "peak_src": f"{pk['src']} bf16 sustained {pk['bf16_tflops_sustained']} TFLOP/s / 2 "
+                                 "(the tf32 dense rate is half the bf16 rate)",
+                     "tf32_pass_frac": round(passes / (tot / 1e3) / 1e12 / peak, 4) if tot else None,
+                     "note": "achieved counts each fp32 GEMM's 2*rows*K*N once; the kernel issues 3 tf32 passes "
+                             "(linear op) or 2 (spike-linear) for fp32 accuracy, tf32_pass_frac counts them"},
+        "kernel_ms_per_chunk": other,
+    }
+
+
+def run_reference_model(args, dist, cfg):
+    """--impl reference for the model: the reference's CPU forward (restated in
+    oracle/, the reference's own PyTorch CPU arithmetic) on a sample of the
+    batch, all host threads, rank 0 only; samples are independent, so tokens/s
+    of the sample is the CPU path's throughput on the whole batch."""
+    model = build_model(cfg, torch.device("cpu"))
+    sd = {k: v.detach() for k, v in model.state_dict().items()}
+    x_all = model_inputs(cfg)
+    n = 2
+    t, _ = time_cpu_model(cfg, sd, x_all, n, steps=args.steps, warmup=args.warmup)
+    seq = cfg["model"]["seq_len"]
+    v = round(n * seq / t, 1)
+    return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: x ~ N(0,1) seeded, random-init weights from torch.manual_seed(0)",
+            "impl": "reference", "config": model_config(cfg, dist.world),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"each step one CPU forward of {n} of the {cfg['batch']} samples"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+NESTED_KEYS = ("value", "unit", "ms_per_step", "config", "step_gbs", "step_hbm_frac", "kernel_ms", "roofline",
+               "gpu_launches", "parity_rel_err", "clocks", "e2e", "cpu_baseline", "scaling")
 
 
 WORKLOADS = {
@@ -623,7 +851,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="spike_linear", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="model_full", choices=sorted(WORKLOADS))
     ap.add_argument("--p", type=float, default=None, help="spike density override")
     ap.add_argument("--branch", default="dense", choices=["auto", "dense", "csr"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -631,6 +859,8 @@ def main():
     ap.add_argument("--eager", action="store_true", help="model workloads: eager forward instead of a CUDA graph")
     ap.add_argument("--rows", type=int, default=None, help="override M (rows per plane) of spike-linear workloads")
     ap.add_argument("--batch", type=int, default=None, help="override B of the attention workload")
+    ap.add_argument("--no-nested", action="store_true",
+                    help="model workload: skip the nested isolated spike-linear measurement")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(WORKLOADS[args.workload])
@@ -649,9 +879,16 @@ def main():
     if args.impl == "reference":
         if dist.rank != 0:
             return
+        if args.workload == "model_full":
+            res = run_reference_model(args, dist, cfg)
+            if not args.no_nested:
+                sub = run_reference_spike_linear(args, dist, dict(WORKLOADS["spike_linear"]))
+                res["spike_linear"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "config", "cpu_baseline")}
+            print(json.dumps(res), flush=True)
+            return
         if args.workload != "spike_linear":
-            print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the default "
-                              "workload only"}))
+            print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the model and "
+                              "the isolated spike-linear workloads only"}))
             return
         print(json.dumps(run_reference_spike_linear(args, dist, cfg)), flush=True)
         return
@@ -668,6 +905,11 @@ def main():
             res = run_layernorm(args, dist, cfg)
         else:
             res = run_model(args, dist, cfg)
+            if args.workload == "model_full" and not args.no_nested:
+                c2 = dict(WORKLOADS["spike_linear"], traffic_profile="spike_linear_dense_c2")
+                sub = run_spike_linear(args, dist, c2)
+                res["spike_linear"] = {k: sub[k] for k in NESTED_KEYS if k in sub}
+                res["gpu_launches"] += sub.get("gpu_launches", 0)
         if dist.rank == 0:
             print(json.dumps(res), flush=True)
     finally:

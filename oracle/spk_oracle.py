@@ -305,6 +305,38 @@ def block_forward(sd, p, x, heads, threshold=0.0):
     return x + ffn_forward(sd, p + ".ffn", h, threshold)
 
 
+def block_stages(sd, p, x, heads, threshold=0.0):
+    """block_forward with its intermediate stages (attention.py:110-117,
+    153-159, 174-177): the two layer-norm outputs h1 and h2, the fp32
+    pre-activations of the q, k, v projections and of fc1, their spikes, the
+    mid-block residual x_mid and the block output.  Spike-flip accounting
+    compares an implementation's spikes, computed from these same h1 / h2,
+    with the ones here."""
+    d = x.shape[-1]
+    st = {}
+    with torch.no_grad():
+        h1 = F.layer_norm(x, (d,), _t(sd[p + ".norm1.weight"]), _t(sd[p + ".norm1.bias"]))
+        st["h1"] = h1
+        a = p + ".attn"
+        st["q_pre"] = _lin(sd, a + ".q_proj", h1)
+        st["k_pre"] = _lin(sd, a + ".k_proj", h1)
+        st["v_pre"] = _lin(sd, a + ".v_proj", h1)
+        st["tau"] = float(np.asarray(sd[a + ".tau"]).reshape(-1)[0])
+        st["q"] = (st["q_pre"] > 0).float()
+        st["k"] = (st["k_pre"] > 0).float()
+        st["v"] = ((torch.tanh(st["v_pre"]) + 1.0) / 2.0 - st["tau"] > 0).float()
+        lam = torch.sigmoid(_t(sd[a + ".decay_logit"]))
+        st["attn"] = spiking_attention(st["q"], st["k"], st["v"], lam, heads)
+        x_mid = x + _lin(sd, a + ".o_proj", st["attn"])
+        st["x_mid"] = x_mid
+        h2 = F.layer_norm(x_mid, (d,), _t(sd[p + ".norm2.weight"]), _t(sd[p + ".norm2.bias"]))
+        st["h2"] = h2
+        st["fc1_pre"] = _lin(sd, p + ".ffn.fc1", h2) - threshold
+        st["act"] = (st["fc1_pre"] > 0).float()
+        st["out"] = x_mid + _lin(sd, fc2_key(sd, p + ".ffn.fc2"), st["act"])
+    return st
+
+
 def transformer_forward(sd, x, num_heads, num_layers, use_gsmc=False, spike_readout=True, threshold=0.0,
                         gsmc_pool="mean", capture=None):
     """SpikingTransformer.forward in temporal mode (transformer.py:159-192).

@@ -23,6 +23,36 @@ def _contig(t):
     return t if t.is_contiguous() else t.contiguous()
 
 
+# (op, rows, K, N) of every dense contraction issued while a tally is open
+_TALLY = None
+
+
+class tally:
+    """Records (op, rows, K, N) of each tensor-core contraction the ops issue
+    inside the ``with`` block -- spike_linear, linear_act and the recurrent
+    projections of gsmc_forward -- so that a caller can count their
+    algorithmic FLOPs (2 * rows * K * N each).  Bookkeeping only."""
+
+    def __enter__(self):
+        global _TALLY
+        self.calls = []
+        _TALLY = self.calls
+        return self
+
+    def __exit__(self, *exc):
+        global _TALLY
+        _TALLY = None
+        return False
+
+    def flops(self):
+        return sum(2.0 * r * k * n for _, r, k, n in self.calls)
+
+
+def _record(op, rows, K, N):
+    if _TALLY is not None:
+        _TALLY.append((op, int(rows), int(K), int(N)))
+
+
 # ----------------------------------------------------------------- spike -> CSR
 def csr_compact(S, values=True):
     """Per-plane CSR of S [T, M, K] (or [M, K] as one plane).
@@ -93,6 +123,7 @@ def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=Non
     c = csr or {}
     cap = c["col_idx"].numel() if c else 0
     ws, wsn = _lib.workspace(S.device, lib.spk_spike_linear_workspace_bytes(T, M, K, N, wdt))
+    _record("spike_linear", T * M, K, N)
     check(lib.spk_spike_linear(ptr(S), T, M, K, ptr(W), wdt, sk, sn, N, ptr(bias), ptr(Y),
                                ptr(c.get("nnz_row")), ptr(c.get("row_ptr")), ptr(c.get("col_idx")),
                                ptr(c.get("values")), ptr(c.get("plane_ptr")), cap, _branch(branch), ws, wsn,
@@ -129,6 +160,7 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
     Y = torch.empty(*x.shape[:-1], N, dtype=torch.float32, device=x.device)
     lib = _lib.load()
     ws, wsn = _lib.workspace(x.device, lib.spk_linear_act_workspace_bytes(K, N))
+    _record("linear_act", R, K, N)
     check(lib.spk_linear_act(ptr(x), R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(bias),
                              _ACTS[act], float(thr), ptr(Y), ws, wsn, stream_of(x)), "spk_linear_act")
     return Y
@@ -306,6 +338,7 @@ def gsmc_forward(gi_all, wd_all, w_rec, bias, v_th=1.0, gate_scale=4.0, adaptive
     planes = torch.empty(T, M, d, dtype=torch.float32, device=gi_all.device) if return_planes else None
     lib = _lib.load()
     ws, wsn = _lib.workspace(gi_all.device, lib.spk_gsmc_workspace_bytes(M, d))
+    _record("gsmc_recurrent", (T - 1) * M, d, 4 * d)  # W_rec s_{t-1} for t >= 1 (s_{-1} = 0 is skipped)
     check(lib.spk_gsmc_forward(ptr(gi_all), ptr(wd_all), ptr(w_rec), ptr(bias), T, M, d, float(v_th),
                                float(gate_scale), int(bool(adaptive)), float(beta), 1 if pool == "mean" else 0,
                                ptr(planes), ptr(pooled), ws, wsn, stream_of(gi_all)), "spk_gsmc_forward")

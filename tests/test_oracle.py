@@ -121,3 +121,18 @@ def test_transformer_matches_reference(golden, name):
     for i in range(cfg["num_layers"]):
         assert O.rel_err(cap[f"block{i}_out"].numpy(), z[f"cap_block{i}_out"]) < 1e-6
     assert O.rel_err(logits.numpy(), z["logits"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["model_c1", "model_c5_tiny"])
+def test_block_stages_match_reference_blocks(golden, name):
+    """The staged block restatement gives the reference's block outputs, and its
+    spikes are the threshold decisions of its own pre-activations."""
+    z = golden(name)
+    cfg = O.model_config_from_golden(z)
+    sd = O.state_dict_from_golden(z)
+    for i in range(cfg["num_layers"]):
+        st = O.block_stages(sd, f"blocks.{i}", torch.from_numpy(z[f"cap_block{i}_in"]), cfg["num_heads"],
+                            cfg.get("spike_threshold", 0.0))
+        np.testing.assert_allclose(st["out"].numpy(), z[f"cap_block{i}_out"], rtol=0, atol=1e-6)
+        assert torch.equal(st["act"], (st["fc1_pre"] > 0).float())
+        assert torch.equal(st["q"], (st["q_pre"] > 0).float())
