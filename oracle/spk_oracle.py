@@ -337,6 +337,20 @@ def block_stages(sd, p, x, heads, threshold=0.0):
     return st
 
 
+def block_from_spikes(sd, p, x, heads, q, k, v, act):
+    """The arithmetic of one block (attention.py:119-136, 158, 174-177) from
+    given q, k, v and fc1 spikes: attn = the normalised attention of (q, k, v),
+    x_mid = x + o_proj(attn), out = x_mid + fc2(act).  With an implementation's
+    own spikes this isolates its arithmetic from its threshold decisions."""
+    a = p + ".attn"
+    with torch.no_grad():
+        lam = torch.sigmoid(_t(sd[a + ".decay_logit"]))
+        attn = spiking_attention(_t(q), _t(k), _t(v), lam, heads)
+        x_mid = _t(x) + _lin(sd, a + ".o_proj", attn)
+        out = x_mid + _lin(sd, fc2_key(sd, p + ".ffn.fc2"), _t(act))
+    return {"attn": attn, "x_mid": x_mid, "out": out}
+
+
 def transformer_forward(sd, x, num_heads, num_layers, use_gsmc=False, spike_readout=True, threshold=0.0,
                         gsmc_pool="mean", capture=None):
     """SpikingTransformer.forward in temporal mode (transformer.py:159-192).

@@ -148,11 +148,15 @@ class AstrocyteHebbianAttention(nn.Module):
                                                 _attn_cuda_engine)
         return out.transpose(-3, -2).contiguous().view(*leading, d)
 
-    def forward(self, x):
+    def forward(self, x, record=None):
+        """``record`` (a dict, optional) receives the q, k, v spikes and the
+        normalised attention ("attn") this call computed."""
         if x.device.type != "cuda":
             raise EngineError("AstrocyteHebbianAttention: CUDA input required (no CPU path)")
         q, k, v = self.spikes(x)
         a = self.attend(q, k, v)
+        if record is not None:
+            record.update(q=q, k=k, v=v, attn=a)
         y = engine_linear(self.o_proj, a)
         return y if y is not None else self.o_proj(a)
 
@@ -171,10 +175,13 @@ class SpikingFFN(nn.Module):
         else:
             self.fc2 = nn.Linear(d_model * expansion, d_model)
 
-    def forward(self, x):
+    def forward(self, x, record=None):
+        """``record`` (a dict, optional) receives the fc1 spikes ("act")."""
         act = engine_linear(self.fc1, x, "heaviside", self.threshold)
         if act is None:
             act = spike_fn(self.fc1(x) - self.threshold)
+        if record is not None:
+            record["act"] = act
         if self.use_spikeskip and x.dim() == 4:
             return self.fc2.forward_multistep(act)
         return self.fc2(act)
@@ -194,18 +201,25 @@ class AstrocyteHebbianBlock(nn.Module):
     def forward(self, x):
         return self.forward_fused(x)[0]
 
-    def forward_fused(self, x, x_norm=None, next_norm=None):
+    def forward_fused(self, x, x_norm=None, next_norm=None, record=None):
         """(block(x), next_norm(block(x)) or None).  At inference each residual
         add runs together with the layer norm of its result (ops.add_layernorm):
         x + attn(.) with norm2, and the block output with `next_norm` (the next
-        block's norm1), whose result the caller hands back as `x_norm`."""
+        block's norm1), whose result the caller hands back as `x_norm`.
+        ``record`` (a dict, optional) receives the stages: q, k, v, attn, the
+        mid-block residual "x_mid" and the fc1 spikes "act"."""
         if not _engine_norm_ok(self.norm1, x):  # the reference's composition (autograd, CPU)
-            x = x + self.attn(self.norm1(x))
-            return x + self.ffn(self.norm2(x)), None
+            x = x + self.attn(self.norm1(x), record)
+            if record is not None:
+                record["x_mid"] = x
+            return x + self.ffn(self.norm2(x), record), None
         if x_norm is None:
             x_norm = ops.add_layernorm(x, None, self.norm1.weight, self.norm1.bias, self.norm1.eps)[1]
-        h, h_norm = ops.add_layernorm(x, self.attn(x_norm), self.norm2.weight, self.norm2.bias, self.norm2.eps)
-        f = self.ffn(h_norm)
+        h, h_norm = ops.add_layernorm(x, self.attn(x_norm, record), self.norm2.weight, self.norm2.bias,
+                                      self.norm2.eps)
+        if record is not None:
+            record["x_mid"] = h
+        f = self.ffn(h_norm, record)
         if next_norm is None:
             return h + f, None
         return ops.add_layernorm(h, f, next_norm.weight, next_norm.bias, next_norm.eps)

