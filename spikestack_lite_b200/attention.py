@@ -16,21 +16,12 @@ import torch
 import torch.nn as nn
 
 from . import ops
+from .ops import engine_linear
 from ._lib import EngineError
 from .engine import attention_engine
 from .sparse import SparseLinear
 
 _attn_cuda_engine = attention_engine
-
-
-def engine_linear(lin, x, act="none", thr=0.0):
-    """act(lin(x)) through the engine's fp32-accurate tensor-core linear
-    (spk_linear_act) when autograd is off and the shape is one it takes
-    (out_features > 64, in_features % 4 == 0); None otherwise, and the caller
-    runs the module (the reference's own nn.Linear, which training needs)."""
-    if torch.is_grad_enabled() or not x.is_cuda or lin.out_features <= 64 or lin.in_features % 4:
-        return None
-    return ops.linear_act(x, lin.weight, lin.bias, act, thr)
 
 
 def _engine_norm_ok(norm, x):

@@ -166,6 +166,16 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
     return Y
 
 
+def engine_linear(lin, x, act="none", thr=0.0):
+    """act(lin(x)) through the engine's fp32-accurate tensor-core linear
+    (spk_linear_act) when autograd is off and the shape is one it takes
+    (out_features > 64, in_features % 4 == 0); None otherwise, and the caller
+    runs the module (the reference's own nn.Linear, which training needs)."""
+    if torch.is_grad_enabled() or not x.is_cuda or lin.out_features <= 64 or lin.in_features % 4:
+        return None
+    return linear_act(x, lin.weight, lin.bias, act, thr)
+
+
 def alloc_csr(T, M, K, device, capacity=None, values=False):
     """Preallocated per-plane CSR buffers for spike_linear(csr=...)."""
     cap = int(capacity if capacity is not None else T * M * K)

@@ -17,6 +17,7 @@ Differences, all deliberate:
 import torch
 
 from . import ops
+from .ops import engine_linear
 from ._lib import EngineError
 from .engine import sparse_engine
 
@@ -140,12 +141,18 @@ class SparseLinear(torch.nn.Module):
         return out.view(T, *leading, self.out_features)
 
     def forward(self, x):
-        """Density-dispatched forward (sparse/__init__.py:264-280): sparse engine
-        for wide layers at >= 90 % sparsity, nn.Linear (cuBLAS) otherwise."""
+        """Density-dispatched forward (sparse/__init__.py:264-280): the
+        spike-linear engine for wide layers (in_features >= sparse_threshold) at
+        >= 90 % sparsity, as the reference; otherwise the reference's dense
+        nn.Linear, run at inference on the engine's fp32-accurate tensor-core
+        linear (spk_linear_act; all values count, negatives included, as in
+        nn.Linear) and through nn.Linear itself under autograd or for shapes
+        that op does not take (out_features <= 64, in_features % 4 != 0)."""
         self._check(x)
         if self.in_features >= self.sparse_threshold:
             with torch.no_grad():
                 nnz = (x != 0).sum().item()
             if 1.0 - nnz / max(1, x.numel()) >= 0.90:
                 return self.forward_multistep(x) if x.dim() >= 3 else self.forward_single(x)
-        return self.linear(x)
+        y = engine_linear(self.linear, x) if x.dtype == torch.float32 else None
+        return y if y is not None else self.linear(x)

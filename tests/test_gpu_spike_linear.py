@@ -266,3 +266,57 @@ def test_full_size_properties():
     assert (Y12 - Y1 - Y2).abs().max().item() / scale < 3e-5
     Yp = ops.spike_linear(S[1:2].contiguous(), weight=W1)
     torch.testing.assert_close(Yp[0], Y1[1], rtol=0, atol=0)
+
+
+def test_sparselinear_forward_dense_side_golden(golden):
+    """SparseLinear.forward below its width threshold (in_features 512 < 1024)
+    takes the reference's dense path -- here the engine's tensor-core linear --
+    and gives the reference module's output (golden mod_y; binary input, so the
+    dense and spike paths agree)."""
+    from spikestack_lite_b200.sparse import SparseLinear
+
+    z = golden("spike_linear")
+    lin = SparseLinear(512, 128, bias=True).cuda()
+    with torch.no_grad():
+        lin.linear.weight.copy_(torch.from_numpy(z["mod_w"]))
+        lin.linear.bias.copy_(torch.from_numpy(z["mod_b"]))
+        x = torch.from_numpy(z["bin_x"]).cuda()
+        y = lin(x)
+        y1 = lin(x[1])  # 2-D input, one plane
+    assert O.rel_err(y.cpu().numpy(), z["mod_y"]) < TOL
+    assert O.rel_err(y1.cpu().numpy(), z["mod_y"][1]) < TOL
+
+
+def test_sparselinear_forward_dense_side_keeps_negative_inputs():
+    """The dense side is nn.Linear's arithmetic: negative inputs count (the
+    spike-linear engine's predicate drops them)."""
+    from spikestack_lite_b200.sparse import SparseLinear
+
+    torch.manual_seed(5)
+    lin = SparseLinear(1024, 96, bias=True).cuda()
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = torch.randn(2, 40, 1024, generator=g, device="cuda")  # dense: sparsity 0 < 0.90
+    with torch.no_grad():
+        y = lin(x)
+    ref = x.cpu().double() @ lin.linear.weight.detach().cpu().double().t() + lin.linear.bias.detach().cpu().double()
+    assert O.rel_err(y.cpu().numpy(), ref.numpy()) < TOL
+
+
+def test_sparselinear_forward_sparse_side_uses_engine():
+    """>= 90 % sparsity at in_features >= 1024: the spike-linear engine, as the
+    reference's forward_multistep / forward_single."""
+    from spikestack_lite_b200 import _lib
+    from spikestack_lite_b200.sparse import SparseLinear
+
+    torch.manual_seed(7)
+    lin = SparseLinear(1024, 128, bias=True).cuda()
+    S = _spikes(3, 200, 1024, 0.05, seed=8)
+    n0 = _lib.launch_count()
+    with torch.no_grad():
+        y = lin(S)
+        y1 = lin(S[0])
+    assert _lib.launch_count() > n0
+    ref = O.spike_linear(S.cpu().numpy(), lin.linear.weight.detach().t().cpu().numpy()) + \
+        lin.linear.bias.detach().cpu().numpy()
+    assert O.rel_err(y.cpu().numpy(), ref) < TOL
+    assert O.rel_err(y1.cpu().numpy(), ref[0]) < TOL
