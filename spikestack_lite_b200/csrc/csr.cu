@@ -89,6 +89,10 @@ struct CsrArgs {
   int KWP;                 // planar words per row (2 per 64-column chunk)
   const int32_t* blk_sum;                // bitmap source: spikes per 128-row block of the T*M rows
   const unsigned long long* sup_sum;     // bitmap source: spikes per 16384-row super-block
+  const int* gate;         // automatic branch choice: run only when *gate == gate_value (null: always)
+  int gate_value;
+  int* decide;             // scan under the automatic choice: the last tile writes SPK_BRANCH_CSR when the
+  int64_t decide_limit;    // total number of spikes is <= decide_limit, else SPK_BRANCH_DENSE (null: none)
 };
 
 // 8 bits -> bits 0, 4, 8, ..., 28
@@ -116,6 +120,7 @@ __device__ __forceinline__ uint64_t spin_desc(const uint64_t* p, bool& ok) {
 }
 
 __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
+  if (gated_off(a.gate, a.gate_value)) return;  // before the tile counter: every block leaves
   extern __shared__ __align__(16) uint32_t smem_u32buf[];
   const int RT = a.rows_per_tile;
   uint32_t* bm = smem_u32buf;                    // [RT][KW]
@@ -217,7 +222,10 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
         const uint64_t d = spin_desc(&a.plane_desc[plane], ok);
         base = (int64_t)(d & kDescValueMask);
       }
-      if (plane == a.T - 1 && tip == a.tiles_per_plane - 1) a.plane_ptr[a.T] = excl + agg;
+      if (plane == a.T - 1 && tip == a.tiles_per_plane - 1) {
+        a.plane_ptr[a.T] = excl + agg;
+        if (a.decide) *a.decide = (excl + agg <= a.decide_limit) ? SPK_BRANCH_CSR : SPK_BRANCH_DENSE;
+      }
       a.tile_flags[tile] = s_nonunit ? 1 : 0;
       s_excl = excl;
       s_base = base;
@@ -292,7 +300,8 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
         pos += __shfl_sync(0xffffffffu, incl, LPR - 1, LPR);
       }
     }
-    if (__any_sync(0xffffffffu, overflow) && lane == 0) report_device_error(SPK_DEV_CSR_OVERFLOW);
+    // under the automatic choice an overflow only means "above the crossover" (the dense branch runs)
+    if (__any_sync(0xffffffffu, overflow) && lane == 0 && a.decide == nullptr) report_device_error(SPK_DEV_CSR_OVERFLOW);
   }
 
 }
@@ -365,6 +374,7 @@ constexpr int kWarpBuf = 1024;                              // column slots stag
 constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
 
 __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
+  if (gated_off(a.gate, a.gate_value)) return;
   extern __shared__ __align__(16) int32_t s_buf_all[];  // [kMaskWarps][kWarpBuf]
   __shared__ int64_t s_red[2 * kMaskWarps];
   __shared__ int s_wtot[kMaskWarps];
@@ -526,11 +536,19 @@ __global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a,
   }
 }
 
+// Gates of the automatic branch choice for the CSR launches (all null: none).
+struct CsrGate {
+  const int* gate = nullptr;
+  int gate_value = 0;
+  int* decide = nullptr;
+  int64_t decide_limit = 0;
+};
+
 int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* row_cnt, const int32_t* blk_sum,
                        const unsigned long long* sup_sum, bool state_zeroed, int T,
                        int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
                        int64_t* plane_ptr, int64_t col_capacity, void* ws, cudaStream_t stream,
-                       const uint8_t** tile_flags_out, CsrLayout* layout_out) {
+                       const uint8_t** tile_flags_out, CsrLayout* layout_out, const CsrGate& gate = CsrGate()) {
   const CsrLayout L = csr_layout(T, M, K);
   CsrArgs a{};
   a.S = S;
@@ -557,6 +575,10 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   a.KWP = 2 * (int)ceil_div(K, 64);
   a.blk_sum = blk_sum;
   a.sup_sum = sup_sum;
+  a.gate = gate.gate;
+  a.gate_value = gate.gate_value;
+  a.decide = gate.decide;
+  a.decide_limit = gate.decide_limit;
   if (bitmap) {
     // follows the dense kernel on the stream: programmatic dependent launch
     const int64_t tpp = ceil_div(M, kMaskRows);
@@ -593,9 +615,10 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
 
 int launch_csr_scan(const float* S, int T, int64_t M, int K, int32_t* nnz_row, int32_t* row_ptr,
                     int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, void* ws,
-                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out) {
+                    cudaStream_t stream, const uint8_t** tile_flags_out, CsrLayout* layout_out,
+                    const CsrGate& gate = CsrGate()) {
   return launch_csr_scan_ex(S, nullptr, nullptr, nullptr, nullptr, false, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
-                            col_capacity, ws, stream, tile_flags_out, layout_out);
+                            col_capacity, ws, stream, tile_flags_out, layout_out, gate);
 }
 
 int check_csr_shape(int T, int64_t M, int K) {

@@ -23,16 +23,88 @@ struct SlLayout {
   size_t csr_planeptr;
   size_t csr_cols;
   int64_t csr_capacity;
+  size_t gate;          // GateWords of the automatic choice
   size_t total;
 };
 
-inline int resolve_branch(int branch, int K, int N, const void* S) {
+// ---------------------------------------------------------------- automatic branch choice
+// Cost model of the two branches on one B200, from the density sweep and the
+// isolated spike-linear measurements of bench.py (rates of whole launches):
+//   dense:  max(HBM bytes / 2.8 TB/s, 2*R*K*N / R_tc), R_tc = 500 TFLOP/s for
+//           bf16 W (one bf16 pass), 290 TFLOP/s for fp32 W (two tf32 passes);
+//   CSR:    the scan reads S at 3.3 TB/s, the SpMM writes Y at 5 TB/s and
+//           performs nnz*N fused multiply-adds at F_csr per second.
+// The CSR branch wins when nnz stays below nnz_limit = (t_dense - t_fixed) *
+// F_csr / N.  The choice is made on the device, without a host round trip
+// (the reference reads the density back with .item(), sparse/__init__.py:268-271).
+constexpr double kDenseHbm = 2.8e12, kTcBf16 = 5.0e14, kTcTf32 = 2.9e14;
+constexpr double kScanHbm = 3.3e12, kYHbm = 5.0e12;
+constexpr double kCsrFmaBf16 = 6.0e12, kCsrFmaF32 = 4.2e12;
+
+inline double csr_nnz_limit(int T, int64_t M, int K, int N, int w_dtype) {
+  const double R = (double)T * (double)M;
+  const double t_dense = fmax(4.0 * R * (K + N) / kDenseHbm, 2.0 * R * K * N / (w_dtype == SPK_BF16 ? kTcBf16 : kTcTf32));
+  const double t_fixed = 4.0 * R * K / kScanHbm + 4.0 * R * N / kYHbm;
+  return (t_dense - t_fixed) * (w_dtype == SPK_BF16 ? kCsrFmaBf16 : kCsrFmaF32) / (double)N;
+}
+
+// Words of the device-side choice in the workspace.
+struct GateWords {
+  int probe;                 // SPK_BRANCH_DENSE or kGateTryCsr (written by the probe)
+  int final_branch;          // SPK_BRANCH_DENSE or SPK_BRANCH_CSR (probe, or the CSR scan's last tile)
+  unsigned long long count;  // positives in the sampled rows
+  unsigned int ticket;       // blocks of the probe that finished
+};
+constexpr int kProbeRows = 1024;
+
+// Counts the positive values of n_rows rows of S spread over all planes (row
+// i * stride), one warp per row; the last block to finish scales the count to
+// the whole input and writes the probe word: clearly above the limit (twice
+// it, far outside the sampling error) -> the dense branch at once, else the
+// CSR scan counts exactly and decides.
+__global__ void __launch_bounds__(256) density_probe_kernel(const float* S, int64_t R, int K, int64_t stride,
+                                                            int n_rows, GateWords* g, double nnz_limit) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  unsigned c = 0;
+  if (row < n_rows) {
+    const float* src = S + (int64_t)row * stride * K;
+    for (int k = lane; k < K; k += 32) c += src[k] > 0.0f ? 1u : 0u;
+  }
+  c = __reduce_add_sync(0xffffffffu, c);
+  if (lane == 0 && c) atomicAdd(&g->count, (unsigned long long)c);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(&g->ticket, 1u) == gridDim.x - 1) {
+    __threadfence();
+    const double est = (double)atomicAdd(&g->count, 0ull) * ((double)R / (double)n_rows);
+    const bool dense = est > 2.0 * nnz_limit;
+    g->probe = dense ? SPK_BRANCH_DENSE : kGateTryCsr;
+    if (dense) g->final_branch = SPK_BRANCH_DENSE;
+  }
+}
+
+inline int launch_density_probe(const float* S, int64_t R, int K, GateWords* g, double nnz_limit,
+                                cudaStream_t stream) {
+  SPK_CUDA_TRY(cudaMemsetAsync(g, 0, sizeof(GateWords), stream));
+  const int n_rows = (int)min64(R, kProbeRows);
+  const int64_t stride = R / n_rows;
+  density_probe_kernel<<<(unsigned)ceil_div(n_rows, 8), 256, 0, stream>>>(S, R, K, stride, n_rows, g, nnz_limit);
+  SPK_LAUNCH_CHECK();
+  count_launch(1);
+  return SPK_OK;
+}
+
+// Branch for this call; *gated = true when the choice is left to the device.
+inline int resolve_branch(int branch, int T, int64_t M, int K, int N, int w_dtype, const void* S, bool* gated) {
+  *gated = false;
   if (branch == SPK_BRANCH_DENSE || branch == SPK_BRANCH_CSR) return branch;
-  // Dense unless the tcgen05 path cannot take the shape.  The dense branch is
-  // HBM-bound for the narrow layers of the model (N <= 512) at any density,
-  // so it never loses there; the CSR branch only wins on wide layers at very
-  // low density, which a caller selects explicitly.
-  return tc_supported(K, N, S) ? SPK_BRANCH_DENSE : SPK_BRANCH_CSR;
+  if (!tc_supported(K, N, S)) return SPK_BRANCH_CSR;  // the tcgen05 path cannot take the shape
+  const double limit = csr_nnz_limit(T, M, K, N, w_dtype);
+  if (limit <= 0.0) return SPK_BRANCH_DENSE;  // the dense branch wins at any density
+  if (limit >= (double)T * (double)M * (double)K) return SPK_BRANCH_CSR;
+  *gated = true;
+  return SPK_BRANCH_AUTO;
 }
 
 inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool internal_csr) {
@@ -63,8 +135,43 @@ inline SlLayout sl_layout(int T, int64_t M, int K, int N, int w_dtype, bool inte
     L.csr_capacity = (int64_t)T * M * K;
     off += align_up(sizeof(int32_t) * (size_t)L.csr_capacity, 256);
   }
+  L.gate = off;
+  off += align_up(sizeof(GateWords), 256);
   L.total = off;
   return L;
+}
+
+// The CSR branch: the scan builds the CSR of all planes (the caller's buffers,
+// or the workspace's), then the SpMM.  Under the automatic choice (gw non-null)
+// the scan runs only when the probe left the choice to it and writes the final
+// branch from the exact spike count; the SpMM runs only when that is the CSR.
+int csr_branch(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t sk, int64_t sn, int N,
+               const float* bias, float* Y, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx, float* values,
+               int64_t* plane_ptr, int64_t col_capacity, bool internal_csr, const SlLayout& L, char* wsb,
+               cudaStream_t stream, GateWords* gw, double nnz_limit) {
+  int32_t* rp = row_ptr;
+  int32_t* ci = col_idx;
+  int64_t* pp = plane_ptr;
+  int64_t cap = col_capacity;
+  if (internal_csr) {
+    rp = reinterpret_cast<int32_t*>(wsb + L.csr_rowptr);
+    pp = reinterpret_cast<int64_t*>(wsb + L.csr_planeptr);
+    ci = reinterpret_cast<int32_t*>(wsb + L.csr_cols);
+    cap = L.csr_capacity;
+  }
+  CsrGate cg;
+  if (gw) {
+    cg.gate = &gw->probe;
+    cg.gate_value = kGateTryCsr;
+    cg.decide = &gw->final_branch;
+    cg.decide_limit = (int64_t)fmin(nnz_limit, (double)cap);  // the CSR branch only when its CSR fits
+  }
+  const uint8_t* flags = nullptr;
+  CsrLayout cl{};
+  int rc = launch_csr_scan(S, T, M, K, nnz_row, rp, ci, values, pp, cap, wsb + L.csr_state, stream, &flags, &cl, cg);
+  if (rc) return rc;
+  return launch_spmm_csr(rp, pp, ci, values, S, flags, cl.rows_per_tile, cl.tiles_per_plane, W, w_dtype, sk, sn,
+                         bias, Y, T, M, K, N, cap, stream, gw ? &gw->final_branch : nullptr);
 }
 
 int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t sk, int64_t sn,
@@ -78,18 +185,31 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
   SPK_REQUIRE(w_dtype == SPK_F32 || w_dtype == SPK_BF16, "w_dtype must be SPK_F32 or SPK_BF16");
   const bool want_csr = row_ptr != nullptr || col_idx != nullptr || plane_ptr != nullptr;
   SPK_REQUIRE(!want_csr || (row_ptr && col_idx && plane_ptr), "CSR outputs need row_ptr, col_idx and plane_ptr");
-  branch = resolve_branch(branch, K, N, S);
-  if (branch == SPK_BRANCH_DENSE) {
+  bool gated = false;
+  branch = resolve_branch(branch, T, M, K, N, w_dtype, S, &gated);
+  if (branch == SPK_BRANCH_DENSE || gated) {
     SPK_REQUIRE(tc_supported(K, N, S), "dense branch needs K %% 4 == 0 and a 16-byte aligned S");
     SPK_REQUIRE((int64_t)T * M < (int64_t(1) << 31), "dense branch: T*M must stay below 2^31 rows (TMA coordinates)");
   }
-  const bool internal_csr = (branch == SPK_BRANCH_CSR) && !want_csr;
+  const bool internal_csr = (branch == SPK_BRANCH_CSR || gated) && !want_csr;
   const SlLayout L = sl_layout(T, M, K, N, w_dtype, internal_csr);
   if (ws == nullptr || ws_bytes < L.total)
     return fail(SPK_EWORKSPACE, "workspace of %zu bytes required (got %zu)", L.total, ws_bytes);
   char* wsb = static_cast<char*>(ws);
+  GateWords* gw = reinterpret_cast<GateWords*>(wsb + L.gate);
+  double nnz_limit = 0.0;
+  if (gated) {
+    // automatic choice on the device: the probe, then both branches, each
+    // of whose kernels returns at once unless the choice is its own
+    nnz_limit = csr_nnz_limit(T, M, K, N, w_dtype);
+    rc = launch_density_probe(S, (int64_t)T * M, K, gw, nnz_limit, stream);
+    if (rc) return rc;
+    rc = csr_branch(S, T, M, K, W, w_dtype, sk, sn, N, bias, Y, nnz_row, row_ptr, col_idx, values, plane_ptr,
+                    col_capacity, internal_csr, L, wsb, stream, gw, nnz_limit);
+    if (rc) return rc;
+  }
 
-  if (branch == SPK_BRANCH_DENSE) {
+  if (branch == SPK_BRANCH_DENSE || gated) {
     // w_image also clears the scan state (tile counter, look-back
     // descriptors, non-unit flag); the dense kernel writes the packed spike
     // bitmap and row counts; the scan expands them (no second read of S).
@@ -104,6 +224,7 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
               : launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream);
     if (rc) return rc;
     TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
+    o.gate = gated ? &gw->final_branch : nullptr;
     if (want_csr) {
       o.bitmap = reinterpret_cast<uint32_t*>(wsb + L.bitmap);
       o.row_cnt = reinterpret_cast<int32_t*>(wsb + L.row_cnt);
@@ -119,30 +240,19 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
     else rc = launch_tc(S, (int64_t)T * M, K, N, p, img, o, stream);
     if (rc) return rc;
     if (want_csr) {
+      CsrGate cg;
+      if (gated) {
+        cg.gate = &gw->final_branch;
+        cg.gate_value = SPK_BRANCH_DENSE;
+      }
       rc = launch_csr_scan_ex(S, o.bitmap, o.row_cnt, o.blk_sum, o.sup_sum, true, T, M, K, nnz_row, row_ptr, col_idx, values, plane_ptr,
-                              col_capacity, wsb + L.csr_state, stream, nullptr, nullptr);
+                              col_capacity, wsb + L.csr_state, stream, nullptr, nullptr, cg);
     }
     return rc;
   }
-  // CSR branch
-  int32_t* rp = row_ptr;
-  int32_t* ci = col_idx;
-  int64_t* pp = plane_ptr;
-  int64_t cap = col_capacity;
-  if (internal_csr) {
-    rp = reinterpret_cast<int32_t*>(wsb + L.csr_rowptr);
-    pp = reinterpret_cast<int64_t*>(wsb + L.csr_planeptr);
-    ci = reinterpret_cast<int32_t*>(wsb + L.csr_cols);
-    cap = L.csr_capacity;
-  }
-  const uint8_t* flags = nullptr;
-  CsrLayout cl{};
-  rc = launch_csr_scan(S, T, M, K, nnz_row, rp, ci, values, pp, cap, wsb + L.csr_state, stream, &flags, &cl);
-  if (rc) return rc;
-  return launch_spmm_csr(rp, pp, ci, values, S, flags, cl.rows_per_tile, cl.tiles_per_plane, W, w_dtype, sk, sn,
-                         bias, Y, T, M, K, N, cap, stream);
+  return csr_branch(S, T, M, K, W, w_dtype, sk, sn, N, bias, Y, nnz_row, row_ptr, col_idx, values, plane_ptr,
+                    col_capacity, internal_csr, L, wsb, stream, nullptr, 0.0);
 }
-
 }  // namespace spk
 
 extern "C" size_t spk_spike_linear_workspace_bytes(int T, int64_t M, int K, int N, int w_dtype) {

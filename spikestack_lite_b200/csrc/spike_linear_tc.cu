@@ -86,11 +86,13 @@ struct TcArgs {
   int32_t* blk_sum;       // spikes per 128-row block (for the CSR scan's prefixes)
   unsigned long long* sup_sum;  // spikes per 16384-row super-block
   float thr;              // threshold of the spiking epilogues of the linear-activation op
+  const int* gate;        // automatic branch choice: run only when *gate == SPK_BRANCH_DENSE (null: always)
 };
 
 template <int NT, bool WSPLIT>
 __global__ void __launch_bounds__(tc::kThreads, 1)
     spike_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
+  if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
   using C = tc::Cfg<NT, WSPLIT>;
   constexpr int G = C::kG, NS = tc::kNS, NA = tc::kNA, NB = tc::kNB;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
@@ -540,6 +542,7 @@ struct TcOut {
   int* nonunit;
   int32_t* blk_sum;
   unsigned long long* sup_sum;
+  const int* gate = nullptr;  // automatic branch choice (see TcArgs::gate)
 };
 
 template <int NT, bool WSPLIT>
@@ -599,6 +602,7 @@ int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.nonunit = o.nonunit;
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
+  a.gate = o.gate;
   if (p.split) {
     switch (p.NT) {
       case 16: return launch_tc_inst<16, true>(map, a, p.n_tiles, stream);

@@ -273,6 +273,7 @@ __device__ __forceinline__ void tf32_converter(const int cw, const int lane, uns
 template <int NT>
 __global__ void __launch_bounds__(t32::kThreads, 1)
     spike_linear_tf32_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
+  if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
   using C = t32::Cfg<NT>;
   constexpr int G = C::kG, NS = t32::kNS, NB = t32::kNB, CW = t32::kConvWarps;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
@@ -609,6 +610,7 @@ int launch_tf32(const float* S, int64_t R, int K, int N, const TcPlan& p, const 
   a.nonunit = o.nonunit;
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
+  a.gate = o.gate;
   switch (p.NT) {
     case 16: return launch_tf32_inst<16>(map, a, p.n_tiles, stream);
     case 32: return launch_tf32_inst<32>(map, a, p.n_tiles, stream);

@@ -156,6 +156,7 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
 template <int kEpi, bool kRelu>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
+  if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
   using RG = wt::Ring<kRelu>;
   constexpr int G = wt::kG, NS = RG::NS, NL = RG::NL, NP = wt::kNP, CW = wt::kConvWarps;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
@@ -510,6 +511,7 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.nonunit = o.nonunit;
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
+  a.gate = o.gate;
   a.thr = thr;
   const int sms = sm_count();
   const int ranges = sms / p.n_tiles > 0 ? sms / p.n_tiles : 1;

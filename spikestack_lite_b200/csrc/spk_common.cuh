@@ -102,6 +102,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void report_device_error(int code) { atomicOr(&g_device_error, code); }
 
+// Device-side branch choice of spike-linear's automatic mode: a kernel given a
+// gate word runs only when the word holds its value (written by earlier
+// kernels of the same stream), otherwise it returns at once.
+constexpr int kGateTryCsr = 3;  // probe word: density may be below the crossover, let the CSR scan decide
+__device__ __forceinline__ bool gated_off(const int* gate, int value) {
+  return gate != nullptr && *reinterpret_cast<const volatile int*>(gate) != value;
+}
+
 // First 1024-byte-aligned byte of a dynamic shared array.  Offsetting the
 // __shared__ array itself (rather than rounding an integer address) keeps the
 // pointer in the shared state space, so accesses through it compile to

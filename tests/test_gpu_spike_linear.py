@@ -320,3 +320,32 @@ def test_sparselinear_forward_sparse_side_uses_engine():
         lin.linear.bias.detach().cpu().numpy()
     assert O.rel_err(y.cpu().numpy(), ref) < TOL
     assert O.rel_err(y1.cpu().numpy(), ref[0]) < TOL
+
+
+@pytest.mark.parametrize("p,expect", [(0.004, "csr"), (0.5, "dense")])
+@pytest.mark.parametrize("wdtype", [torch.bfloat16, torch.float32])
+def test_auto_branch_choice_on_device(p, expect, wdtype):
+    """branch="auto" decides on the device (density probe, then the CSR scan's
+    exact count against the crossover): far below the crossover it runs the
+    CSR branch, far above it the dense branch.  The two branches round
+    differently, so bit-equality with the explicit branch's output shows which
+    one ran; the per-plane CSR outputs are exact either way."""
+    T, M, K, N = 2, 3000, 2048, 512
+    S = _spikes(T, M, K, p, seed=int(p * 1e4))
+    W = _weight(N, K, seed=9, dtype=wdtype)
+    b = torch.randn(N, device="cuda")
+    want = ops.spike_linear(S, weight=W, bias=b, branch=expect)
+    other = ops.spike_linear(S, weight=W, bias=b, branch="dense" if expect == "csr" else "csr")
+    assert not torch.equal(want, other)  # the test can tell the branches apart
+    csr = ops.alloc_csr(T, M, K, "cuda")
+    got = ops.spike_linear(S, weight=W, bias=b, branch="auto", csr=csr)
+    assert torch.equal(got, want), f"auto did not take the {expect} branch at p={p}"
+    got2 = ops.spike_linear(S, weight=W, bias=b, branch="auto")  # internal CSR
+    assert torch.equal(got2, want)
+    exp = O.csr_planes(S.cpu().numpy())
+    n = int(exp[4][-1])
+    assert csr["plane_ptr"].cpu().numpy().tolist() == exp[4].tolist()
+    np.testing.assert_array_equal(csr["row_ptr"].cpu().numpy().reshape(T, M + 1), exp[1])
+    np.testing.assert_array_equal(csr["col_idx"][:n].cpu().numpy(), exp[2])
+    ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy()) + b.cpu().numpy()
+    assert O.rel_err(got.cpu().numpy(), ref) < TOL
