@@ -797,6 +797,66 @@ def model_roofline(prof, tl, mc):
     }
 
 
+def run_crossover(args, dist, cfg):
+    """Density sweep S[4, 65536, 2048], W[2048, 2048] bf16: step time of the
+    dense branch, the CSR branch and the automatic choice at each density
+    (each step replayed from a CUDA graph over two rotating input sets of
+    2.1 GB each, CUDA events)."""
+    from spikestack_lite_b200 import _lib, ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    T, M, K, N = cfg["T"], cfg["M"], cfg["K"], cfg["N"]
+    g = torch.Generator(device=dev).manual_seed(77 + dist.rank)
+    W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+    pk = peaks()
+    table = []
+    for p in cfg["densities"]:
+        sets = [(torch.rand(T, M, K, generator=g, device=dev) < p).float() for _ in range(2)]
+        nnz = statistics.mean(int((S > 0).sum().item()) for S in sets)
+        row = {"p": p, "nnz": int(nnz)}
+        for br in ("dense", "csr", "auto"):
+            for i in range(2):
+                ops.spike_linear(sets[i], weightT=W, branch=br)
+            torch.cuda.synchronize()
+            graphs = []
+            for i in range(2):
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph):
+                    ops.spike_linear(sets[i], weightT=W, branch=br)
+                graphs.append(gph)
+            steps = args.steps
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for i in range(2):
+                graphs[i].replay()
+            torch.cuda.synchronize()
+            start.record()
+            for i in range(steps):
+                graphs[i % 2].replay()
+            stop.record()
+            torch.cuda.synchronize()
+            row[f"{br}_ms"] = round(dist.max(start.elapsed_time(stop)) / steps, 4)
+            del graphs
+        _lib.profile_begin("dense")
+        for i in range(3):
+            ops.spike_linear(sets[i % 2], weightT=W, branch="dense")
+        tot, n = _lib.profile_end()
+        dense_kernel_ms = tot / max(n, 1)
+        row["dense_kernel_tflops"] = round(2.0 * T * M * K * N / (dense_kernel_ms / 1e3) / 1e12, 1)
+        row["dense_tensor_frac"] = round(row["dense_kernel_tflops"] / pk["bf16_tflops"], 4)
+        row["faster"] = "csr" if row["csr_ms"] < row["dense_ms"] else "dense"
+        row["auto_took"] = "csr" if abs(row["auto_ms"] - row["csr_ms"]) < abs(row["auto_ms"] - row["dense_ms"]) else "dense"
+        row["gsops"] = round(nnz * N / (min(row["auto_ms"], 1e9) / 1e3) / 1e9, 1)
+        table.append(row)
+        del sets
+        torch.cuda.empty_cache()
+    return {"metric": METRIC, "value": None, "unit": "ms", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "dtype": "bf16 W, fp32 S / accumulate",
+            "data": "synthetic", "config": {"workload": cfg["name"], "T": T, "M": M, "K": K, "N": N,
+                                            "timing": "CUDA graph per input set (2 sets of 2.1 GB), CUDA events"},
+            "peak_bf16_tflops": pk["bf16_tflops"], "crossover": table}
+
+
 def run_reference_model(args, dist, cfg):
     """--impl reference for the model: the reference's CPU forward (restated in
     oracle/, the reference's own PyTorch CPU arithmetic) on a sample of the
@@ -828,6 +888,9 @@ WORKLOADS = {
                      "T": 3, "M": 16384, "K": 512, "N": 128, "p": 0.10, "w_dtype": "f32", "csr": True},
     "sweep": {"name": "spike-linear density sweep S[4,65536,2048], W[2048,2048] bf16", "T": 4, "M": 65536,
               "K": 2048, "N": 2048, "p": 0.10, "w_dtype": "bf16", "csr": False},
+    "crossover": {"name": "spike-linear density sweep S[4,65536,2048], W[2048,2048] bf16: dense vs CSR vs auto",
+                  "T": 4, "M": 65536, "K": 2048, "N": 2048,
+                  "densities": [0.01, 0.02, 0.05, 0.1, 0.2, 0.35, 0.5]},
     "linear": {"name": "C5 SpikingFFN fc1 + threshold spike: x[4*512*1024, 512] -> [.., 2048]", "R": 4 * 512 * 1024,
                "rows_per_batch": 4 * 1024, "K": 512, "N": 2048, "thr": 0.0},
     "attention": {"name": "spiking linear attention B=64 H=8 L=4096 dh=64 T=4 p=0.15", "T": 4, "B": 64,
@@ -897,6 +960,8 @@ def main():
     try:
         if args.workload in ("spike_linear", "sweep"):
             res = run_spike_linear(args, dist, cfg)
+        elif args.workload == "crossover":
+            res = run_crossover(args, dist, cfg)
         elif args.workload == "attention":
             res = run_attention(args, dist, cfg)
         elif args.workload == "linear":

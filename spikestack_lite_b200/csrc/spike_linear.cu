@@ -39,7 +39,7 @@ struct SlLayout {
 // (the reference reads the density back with .item(), sparse/__init__.py:268-271).
 constexpr double kDenseHbm = 2.8e12, kTcBf16 = 5.0e14, kTcTf32 = 2.9e14;
 constexpr double kScanHbm = 3.3e12, kYHbm = 5.0e12;
-constexpr double kCsrFmaBf16 = 6.0e12, kCsrFmaF32 = 4.2e12;
+constexpr double kCsrFmaBf16 = 7.0e12, kCsrFmaF32 = 4.2e12;
 
 inline double csr_nnz_limit(int T, int64_t M, int K, int N, int w_dtype) {
   const double R = (double)T * (double)M;

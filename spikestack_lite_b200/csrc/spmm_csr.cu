@@ -128,8 +128,8 @@ __device__ __forceinline__ void load_wvec(const WT* wr, float (&w)[VEC]) {
 
 // acc += w for unit spikes, VEC columns from one 16-byte gather, bit-identical
 // to fmaf(1.0f, w, acc): bf16 W by the mixed-precision fma.rn.f32.bf16 on the
-// packed halves (the product 1 x w is exact), fp32 W by the packed
-// fma.rn.f32x2 (two independent fp32 fmas per instruction).
+// packed halves (the product 1 x w is exact, so no conversion instructions),
+// fp32 W by plain adds (1 x w + acc rounds once either way).
 template <typename WT, int VEC>
 __device__ __forceinline__ void acc_unit(const WT* wr, float (&acc)[VEC]) {
   const uint4 q = *reinterpret_cast<const uint4*>(wr);
@@ -146,15 +146,7 @@ __device__ __forceinline__ void acc_unit(const WT* wr, float (&acc)[VEC]) {
           : "r"(word[i]));
   } else {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      unsigned long long c = (unsigned long long)__float_as_uint(acc[2 * i]) |
-                             ((unsigned long long)__float_as_uint(acc[2 * i + 1]) << 32);
-      const unsigned long long w = (unsigned long long)word[2 * i] | ((unsigned long long)word[2 * i + 1] << 32);
-      const unsigned long long one2 = 0x3f8000003f800000ull;
-      asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(one2), "l"(w));
-      acc[2 * i] = __uint_as_float((uint32_t)c);
-      acc[2 * i + 1] = __uint_as_float((uint32_t)(c >> 32));
-    }
+    for (int i = 0; i < 4; ++i) acc[i] += __uint_as_float(word[i]);  // fmaf(1, w, acc) == acc + w
   }
 }
 
