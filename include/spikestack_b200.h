@@ -146,6 +146,23 @@ int spk_spike_linear(const float* S, int T, int64_t M, int K, const void* W, int
                      int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity, int branch,
                      void* workspace, size_t workspace_bytes, spk_stream_t stream);
 
+/* Prepared weights.  The dense branch reads W through a weight image (tf32
+ * hi + lo pieces for fp32 W, K-major bf16 blocks for bf16 W) that
+ * spk_spike_linear and spk_linear_act rebuild from W on every call.  A caller
+ * whose weights stay fixed between calls (inference) builds the image once
+ * with spk_weight_image (image: 1024-byte aligned, spk_weight_image_bytes
+ * bytes) and passes it to the *_img variants, which skip the rebuild; W is
+ * still read by the CSR branch.  w_image = NULL behaves as the plain entry
+ * point.  No counterpart in the reference (its ops take weightT on every call,
+ * sparse/__init__.py:148-162); it replaces the per-call weight transpose. */
+size_t spk_weight_image_bytes(int K, int N, int w_dtype);
+int spk_weight_image(const void* W, int w_dtype, int64_t w_stride_k, int64_t w_stride_n, int K, int N, void* image,
+                     size_t image_bytes, spk_stream_t stream);
+int spk_spike_linear_img(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t w_stride_k,
+                         int64_t w_stride_n, int N, const void* w_image, const float* bias, float* Y, int32_t* nnz_row,
+                         int32_t* row_ptr, int32_t* col_idx, float* values, int64_t* plane_ptr, int64_t col_capacity,
+                         int branch, void* workspace, size_t workspace_bytes, spk_stream_t stream);
+
 /* Reference-compatible ops.  Same arguments and results as the reference's
  * pybind ops sparse_forward (sparse_linear.cu:594-631) and
  * sparse_multistep_forward (sparse_linear.cu:645-691): input [B, I] /
@@ -179,6 +196,11 @@ size_t spk_linear_act_workspace_bytes(int K, int N);
 int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n, int N,
                    const float* bias, int act, float thr, float* Y, void* workspace, size_t workspace_bytes,
                    spk_stream_t stream);
+/* spk_linear_act with a weight image prepared by spk_weight_image (fp32 W);
+ * the workspace may then be NULL. */
+int spk_linear_act_img(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n,
+                       int N, const void* w_image, const float* bias, int act, float thr, float* Y, void* workspace,
+                       size_t workspace_bytes, spk_stream_t stream);
 
 /* ------------------------------------------------------- attention
  * apply_channel_decay (attention_cuda.cu:7-77, attention.py:30-44):

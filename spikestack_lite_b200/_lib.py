@@ -39,6 +39,11 @@ SIGNATURES = {
     "spk_linear_act_workspace_bytes": (_Z, [_I, _I]),
     "spk_linear_act": (_I, [_P, _L, _I, _P, _L, _L, _I, _P, _I, _F, _P, _P, _Z, _P]),
     "spk_spike_linear": (_I, [_P, _I, _L, _I, _P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _L, _I, _P, _Z, _P]),
+    "spk_weight_image_bytes": (_Z, [_I, _I, _I]),
+    "spk_weight_image": (_I, [_P, _I, _L, _L, _I, _I, _P, _Z, _P]),
+    "spk_spike_linear_img": (_I, [_P, _I, _L, _I, _P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _I, _P, _Z,
+                                  _P]),
+    "spk_linear_act_img": (_I, [_P, _L, _I, _P, _L, _L, _I, _P, _P, _I, _F, _P, _P, _Z, _P]),
     "spk_sparse_forward_workspace_bytes": (_Z, [_I, _L, _I, _I]),
     "spk_sparse_forward": (_I, [_P, _L, _I, _P, _I, _P, _P, _P, _P, _L, _P, _I, _P, _Z, _P]),
     "spk_sparse_multistep_forward": (_I, [_P, _I, _L, _I, _P, _I, _P, _P, _P, _P, _L, _P, _I, _P, _Z, _P]),

@@ -77,10 +77,7 @@ int launch_gsmc_step(const float* gi, const float* gr, const float* wd, const fl
   return SPK_OK;
 }
 
-int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t sk, int64_t sn,
-                      int N, const float* bias, float* Y, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx,
-                      float* values, int64_t* plane_ptr, int64_t col_capacity, int branch, void* ws,
-                      size_t ws_bytes, cudaStream_t stream);
+// spike_linear_impl (spike_linear.cu, earlier in this translation unit) runs the recurrent projection.
 
 struct GsmcLayout {
   size_t m, s, heat, gr, sl, sl_bytes, total;

@@ -177,7 +177,7 @@ int csr_branch(const float* S, int T, int64_t M, int K, const void* W, int w_dty
 int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, int w_dtype, int64_t sk, int64_t sn,
                       int N, const float* bias, float* Y, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx,
                       float* values, int64_t* plane_ptr, int64_t col_capacity, int branch, void* ws,
-                      size_t ws_bytes, cudaStream_t stream) {
+                      size_t ws_bytes, cudaStream_t stream, const unsigned char* w_img = nullptr) {
   int rc = check_csr_shape(T, M, K);
   if (rc) return rc;
   SPK_REQUIRE(N >= 1, "N must be positive");
@@ -220,11 +220,17 @@ int spike_linear_impl(const float* S, int T, int64_t M, int K, const void* W, in
     // fp32 W: tf32 kernel (spikes read by the tensor cores straight from the
     // TMA staging); bf16 W: bf16 kernel (one MMA per k-step, no W split)
     const bool tf32 = w_dtype == SPK_F32;
-    rc = tf32 ? launch_w_image_tf32(W, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream)
-              : launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream);
-    if (rc) return rc;
+    if (w_img != nullptr) {  // prepared by spk_weight_image: only the CSR pass state needs clearing
+      img = const_cast<unsigned char*>(w_img);
+      if (zero_words) SPK_CUDA_TRY(cudaMemsetAsync(state, 0, (size_t)zero_words * 4, stream));
+    } else {
+      rc = tf32 ? launch_w_image_tf32(W, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream)
+                : launch_w_image(W, w_dtype, sk, sn, K, N, p, img, want_csr ? state : nullptr, zero_words, stream);
+      if (rc) return rc;
+    }
     TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
     o.gate = gated ? &gw->final_branch : nullptr;
+    o.early_s = w_img == nullptr ? 1 : 0;
     if (want_csr) {
       o.bitmap = reinterpret_cast<uint32_t*>(wsb + L.bitmap);
       o.row_cnt = reinterpret_cast<int32_t*>(wsb + L.row_cnt);
@@ -269,6 +275,45 @@ extern "C" int spk_spike_linear(const float* S, int T, int64_t M, int K, const v
   return spk::spike_linear_impl(S, T, M, K, W, w_dtype, w_stride_k, w_stride_n, N, bias, Y, nnz_row, row_ptr,
                                 col_idx, values, plane_ptr, col_capacity, branch, workspace, workspace_bytes,
                                 (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- prepared weights
+// The dense branch reads W through a weight image (tf32 hi + lo pieces for
+// fp32 W, the bf16 K-major blocks for bf16 W), rebuilt from W on every call
+// by default.  A caller whose weights do not change between calls (inference)
+// builds it once and passes it to the *_img entry points.
+extern "C" size_t spk_weight_image_bytes(int K, int N, int w_dtype) {
+  if (K < 1 || N < 1 || (w_dtype != SPK_F32 && w_dtype != SPK_BF16)) return 0;
+  const spk::TcPlan p = spk::tc_plan(K, N, w_dtype);
+  return spk::align_up(w_dtype == SPK_F32 ? spk::tf32_img_bytes(p) : p.img_bytes, 1024);
+}
+
+extern "C" int spk_weight_image(const void* W, int w_dtype, int64_t w_stride_k, int64_t w_stride_n, int K, int N,
+                                void* image, size_t image_bytes, spk_stream_t stream) {
+  using namespace spk;
+  SPK_REQUIRE(W && image, "W and image must be non-null");
+  SPK_REQUIRE(K >= 1 && N >= 1, "bad shape K=%d N=%d", K, N);
+  SPK_REQUIRE(w_dtype == SPK_F32 || w_dtype == SPK_BF16, "w_dtype must be SPK_F32 or SPK_BF16");
+  const size_t need = spk_weight_image_bytes(K, N, w_dtype);
+  if (image_bytes < need) return fail(SPK_EWORKSPACE, "weight image of %zu bytes required (got %zu)", need, image_bytes);
+  SPK_REQUIRE((reinterpret_cast<uintptr_t>(image) & 1023) == 0, "the weight image must be 1024-byte aligned");
+  const TcPlan p = tc_plan(K, N, w_dtype);
+  unsigned char* img = static_cast<unsigned char*>(image);
+  cudaStream_t st = (cudaStream_t)stream;
+  return w_dtype == SPK_F32 ? launch_w_image_tf32(W, w_stride_k, w_stride_n, K, N, p, img, nullptr, 0, st)
+                            : launch_w_image(W, w_dtype, w_stride_k, w_stride_n, K, N, p, img, nullptr, 0, st);
+}
+
+extern "C" int spk_spike_linear_img(const float* S, int T, int64_t M, int K, const void* W, int w_dtype,
+                                    int64_t w_stride_k, int64_t w_stride_n, int N, const void* w_image,
+                                    const float* bias, float* Y, int32_t* nnz_row, int32_t* row_ptr, int32_t* col_idx,
+                                    float* values, int64_t* plane_ptr, int64_t col_capacity, int branch,
+                                    void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  SPK_REQUIRE(w_image == nullptr || (reinterpret_cast<uintptr_t>(w_image) & 1023) == 0,
+              "the weight image must be 1024-byte aligned");
+  return spk::spike_linear_impl(S, T, M, K, W, w_dtype, w_stride_k, w_stride_n, N, bias, Y, nnz_row, row_ptr,
+                                col_idx, values, plane_ptr, col_capacity, branch, workspace, workspace_bytes,
+                                (cudaStream_t)stream, static_cast<const unsigned char*>(w_image));
 }
 
 extern "C" size_t spk_sparse_forward_workspace_bytes(int T, int64_t B, int I, int O) {
@@ -328,9 +373,29 @@ extern "C" size_t spk_linear_act_workspace_bytes(int K, int N) {
   return spk::align_up(spk::tf32_img_bytes(spk::tc_plan(K, N, SPK_F32)), 1024);
 }
 
+static int linear_act_impl(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n,
+                           int N, const void* w_image, const float* bias, int act, float thr, float* Y, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream);
+
 extern "C" int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k,
                               int64_t w_stride_n, int N, const float* bias, int act, float thr, float* Y,
                               void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  return linear_act_impl(X, R, K, W, w_stride_k, w_stride_n, N, nullptr, bias, act, thr, Y, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int spk_linear_act_img(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k,
+                                  int64_t w_stride_n, int N, const void* w_image, const float* bias, int act,
+                                  float thr, float* Y, void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  SPK_REQUIRE(w_image == nullptr || (reinterpret_cast<uintptr_t>(w_image) & 1023) == 0,
+              "the weight image must be 1024-byte aligned");
+  return linear_act_impl(X, R, K, W, w_stride_k, w_stride_n, N, w_image, bias, act, thr, Y, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
+}
+
+static int linear_act_impl(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n,
+                           int N, const void* w_image, const float* bias, int act, float thr, float* Y, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream) {
   using namespace spk;
   SPK_REQUIRE(R >= 0 && K >= 1 && N >= 1, "bad shape R=%lld K=%d N=%d", (long long)R, K, N);
   SPK_REQUIRE(R < (int64_t(1) << 31), "linear_act: at most 2^31 - 1 rows per call (TMA row coordinates)");
@@ -340,13 +405,18 @@ extern "C" int spk_linear_act(const float* X, int64_t R, int K, const float* W, 
   SPK_REQUIRE(K % 4 == 0 && (R == 0 || tc_supported(K, N, X)), "linear_act needs K %% 4 == 0 and a 16-byte aligned X");
   const TcPlan p = tc_plan(K, N, SPK_F32);
   const size_t need = align_up(tf32_img_bytes(p), 1024);
-  if (workspace == nullptr || workspace_bytes < need)
+  if (w_image == nullptr && (workspace == nullptr || workspace_bytes < need))
     return fail(SPK_EWORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
   if (R == 0) return SPK_OK;
   unsigned char* img = static_cast<unsigned char*>(workspace);
-  cudaStream_t st = (cudaStream_t)stream;
-  int rc = launch_w_image_tf32(W, w_stride_k, w_stride_n, K, N, p, img, nullptr, 0, st);
-  if (rc) return rc;
+  cudaStream_t st = stream;
+  if (w_image != nullptr) {
+    img = static_cast<unsigned char*>(const_cast<void*>(w_image));
+  } else {
+    int rc = launch_w_image_tf32(W, w_stride_k, w_stride_n, K, N, p, img, nullptr, 0, st);
+    if (rc) return rc;
+  }
   TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
+  o.early_s = w_image == nullptr ? 1 : 0;
   return launch_wt(X, R, K, N, p, img, o, st, act, thr);
 }

@@ -87,6 +87,8 @@ struct TcArgs {
   unsigned long long* sup_sum;  // spikes per 16384-row super-block
   float thr;              // threshold of the spiking epilogues of the linear-activation op
   const int* gate;        // automatic branch choice: run only when *gate == SPK_BRANCH_DENSE (null: always)
+  int early_s;            // 1: the weight-image kernel (a plain launch) directly precedes this programmatic
+                          // dependent, so S is complete and may be read before griddepcontrol.wait
 };
 
 template <int NT, bool WSPLIT>
@@ -543,6 +545,7 @@ struct TcOut {
   int32_t* blk_sum;
   unsigned long long* sup_sum;
   const int* gate = nullptr;  // automatic branch choice (see TcArgs::gate)
+  int early_s = 1;            // the weight-image kernel precedes the launch (see TcArgs::early_s)
 };
 
 template <int NT, bool WSPLIT>
@@ -603,6 +606,7 @@ int launch_tc(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
   a.gate = o.gate;
+  a.early_s = o.early_s;
   if (p.split) {
     switch (p.NT) {
       case 16: return launch_tc_inst<16, true>(map, a, p.n_tiles, stream);

@@ -333,12 +333,13 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Programmatic dependent of the weight-image kernel (image + cleared scan
-  // state).  That kernel is a plain launch, so S was complete before it
-  // started: the producer requests the first slots of S before its wait, and
-  // the converters screen them before theirs (ahead of their first global
-  // write).
-  const bool late_dep = (warp == 0 && lane == 0) || (warp >= 2 && warp < 2 + CW);
+  // Programmatic dependent of the kernel before it.  When that is the
+  // weight-image kernel (a plain launch, so S was complete before it
+  // started; a.early_s) the producer requests the first slots of S before its
+  // wait, and the converters screen them before theirs (ahead of their first
+  // global write); otherwise (a prepared image: the previous kernel may be
+  // the one writing S) every warp waits first.
+  const bool late_dep = a.early_s && ((warp == 0 && lane == 0) || (warp >= 2 && warp < 2 + CW));
   if (!late_dep) asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
@@ -358,8 +359,8 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
           tma_load_2d(dst + t32::kAtomBytes, &tmap_s, kc * t32::kKChunk + 32, y, &stg_full[s]);
         }
       };
-      int pre = 0;  // slots requested before the wait: the first NS (or all)
-      for (int g = 0; g < groups && pre < NS; ++g) {
+      int pre = 0;  // slots requested before the wait: the first NS (or all), only when S is known complete
+      for (int g = 0; g < groups && pre < NS && a.early_s; ++g) {
         const int tg = min(G, tiles - g * G);
         for (int kc = 0; kc < nk && pre < NS; ++kc)
           for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(g * G + t) * t32::kRows, kc);
@@ -611,6 +612,7 @@ int launch_tf32(const float* S, int64_t R, int K, int N, const TcPlan& p, const 
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
   a.gate = o.gate;
+  a.early_s = o.early_s;
   switch (p.NT) {
     case 16: return launch_tf32_inst<16>(map, a, p.n_tiles, stream);
     case 32: return launch_tf32_inst<32>(map, a, p.n_tiles, stream);

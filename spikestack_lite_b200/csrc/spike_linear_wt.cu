@@ -228,11 +228,13 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Programmatic dependent of the weight-image kernel (image + cleared scan
-  // state).  That kernel is a plain launch, so S was complete before it
-  // started: the S producer requests the first slots before its wait, and the
-  // converters screen them before theirs (ahead of their first global write).
-  const bool late_dep = (warp == 0 && lane == 0) || (warp >= 3 && warp < 3 + CW);
+  // Programmatic dependent of the kernel before it.  When that is the
+  // weight-image kernel (a plain launch, so S was complete before it started;
+  // a.early_s) the S producer requests the first slots before its wait, and
+  // the converters screen them before theirs (ahead of their first global
+  // write); otherwise (a prepared image: the previous kernel may be the one
+  // writing S) every warp waits first.
+  const bool late_dep = a.early_s && ((warp == 0 && lane == 0) || (warp >= 3 && warp < 3 + CW));
   if (!late_dep) asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
@@ -252,8 +254,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           tma_load_2d(dst + wt::kAtomBytes, &tmap_s, kc * wt::kKChunk + 32, y, &stg_full[s]);
         }
       };
-      int pre = 0;  // slots requested before the wait: the first NS (or all)
-      for (int g = 0; g < groups && pre < NS; ++g) {
+      int pre = 0;  // slots requested before the wait: the first NS (or all), only when S is known complete
+      for (int g = 0; g < groups && pre < NS && a.early_s; ++g) {
         const int tg = min(G, tiles - g * G);
         for (int kc = 0; kc < nk && pre < NS; ++kc)
           for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(g * G + t) * wt::kRows, kc);
@@ -512,6 +514,7 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   a.blk_sum = o.blk_sum;
   a.sup_sum = o.sup_sum;
   a.gate = o.gate;
+  a.early_s = o.early_s;
   a.thr = thr;
   const int sms = sm_count();
   const int ranges = sms / p.n_tiles > 0 ? sms / p.n_tiles : 1;

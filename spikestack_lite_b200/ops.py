@@ -4,6 +4,8 @@ Every op validates its tensors (CUDA, float32, contiguous where the kernel
 needs it), passes raw pointers and the current stream of the tensors' device
 to libspk_b200.so and raises ``EngineError`` (a RuntimeError) on any failure.
 """
+import weakref
+
 import torch
 
 from . import _lib
@@ -51,6 +53,55 @@ class tally:
 def _record(op, rows, K, N):
     if _TALLY is not None:
         _TALLY.append((op, int(rows), int(K), int(N)))
+
+
+# ------------------------------------------------------------ prepared weights
+# The dense branch reads W through a weight image (spk_weight_image) that the
+# plain entry points rebuild from W on every call.  Weights that stay fixed
+# between calls (inference) get theirs built once: the cache holds one image
+# per live weight tensor, valid while the tensor object, its version counter
+# (bumped by every in-place change), pointer, shape, strides and dtype are
+# unchanged, and drops it when the tensor is freed.  A weight changed through
+# `.data` escapes the version counter: call clear_weight_cache() after that.
+_IMG = {}
+_IMG_ENABLED = True
+
+
+def set_weight_cache(enabled):
+    """Turn the prepared-weight cache on or off (on by default)."""
+    global _IMG_ENABLED
+    _IMG_ENABLED = bool(enabled)
+    if not _IMG_ENABLED:
+        _IMG.clear()
+
+
+def clear_weight_cache():
+    _IMG.clear()
+
+
+def _weight_image(W, K, N, sk, sn, wdt):
+    """The cached weight image of W (a 1024-byte aligned uint8 view), or None
+    (cache off, or a stream capture in progress: an image built there would
+    hold nothing until the graph is replayed)."""
+    if not _IMG_ENABLED:
+        return None
+    key = (W.data_ptr(), tuple(W.shape), tuple(W.stride()), W.dtype, int(sk), int(sn), int(K), int(N))
+    ent = _IMG.get(id(W))
+    if ent is not None:
+        ref, ver, k, img = ent
+        if ref() is W and ver == W._version and k == key:
+            return img
+    if torch.cuda.is_current_stream_capturing():
+        return None
+    lib = _lib.load()
+    nbytes = int(lib.spk_weight_image_bytes(K, N, wdt))
+    buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=W.device)
+    off = (-buf.data_ptr()) % 1024
+    img = buf[off:off + nbytes]
+    check(lib.spk_weight_image(ptr(W), wdt, sk, sn, K, N, ptr(img), nbytes, stream_of(W)), "spk_weight_image")
+    wid = id(W)
+    _IMG[wid] = (weakref.ref(W, lambda _r, i=wid: _IMG.pop(i, None)), W._version, key, img)
+    return img
 
 
 # ----------------------------------------------------------------- spike -> CSR
@@ -124,10 +175,11 @@ def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=Non
     cap = c["col_idx"].numel() if c else 0
     ws, wsn = _lib.workspace(S.device, lib.spk_spike_linear_workspace_bytes(T, M, K, N, wdt))
     _record("spike_linear", T * M, K, N)
-    check(lib.spk_spike_linear(ptr(S), T, M, K, ptr(W), wdt, sk, sn, N, ptr(bias), ptr(Y),
-                               ptr(c.get("nnz_row")), ptr(c.get("row_ptr")), ptr(c.get("col_idx")),
-                               ptr(c.get("values")), ptr(c.get("plane_ptr")), cap, _branch(branch), ws, wsn,
-                               stream_of(S)), "spk_spike_linear")
+    img = _weight_image(W, K, N, sk, sn, wdt) if _branch(branch) != _lib.BRANCH_CSR else None
+    check(lib.spk_spike_linear_img(ptr(S), T, M, K, ptr(W), wdt, sk, sn, N, ptr(img), ptr(bias), ptr(Y),
+                                   ptr(c.get("nnz_row")), ptr(c.get("row_ptr")), ptr(c.get("col_idx")),
+                                   ptr(c.get("values")), ptr(c.get("plane_ptr")), cap, _branch(branch), ws, wsn,
+                                   stream_of(S)), "spk_spike_linear")
     return Y[0] if squeeze else Y
 
 
@@ -161,8 +213,9 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
     lib = _lib.load()
     ws, wsn = _lib.workspace(x.device, lib.spk_linear_act_workspace_bytes(K, N))
     _record("linear_act", R, K, N)
-    check(lib.spk_linear_act(ptr(x), R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(bias),
-                             _ACTS[act], float(thr), ptr(Y), ws, wsn, stream_of(x)), "spk_linear_act")
+    img = _weight_image(weight, K, N, weight.stride(1), weight.stride(0), _lib.SPK_F32)
+    check(lib.spk_linear_act_img(ptr(x), R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(img),
+                                 ptr(bias), _ACTS[act], float(thr), ptr(Y), ws, wsn, stream_of(x)), "spk_linear_act")
     return Y
 
 

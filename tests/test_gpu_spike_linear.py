@@ -349,3 +349,76 @@ def test_auto_branch_choice_on_device(p, expect, wdtype):
     np.testing.assert_array_equal(csr["col_idx"][:n].cpu().numpy(), exp[2])
     ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy()) + b.cpu().numpy()
     assert O.rel_err(got.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
+def test_prepared_weight_image_cache(wdtype):
+    """The dense branch with a weight image prepared once (ops' cache) gives
+    exactly the per-call rebuild's output, and an in-place weight change (a new
+    version) rebuilds it."""
+    S = _spikes(3, 700, 512, 0.1, seed=31)
+    W = _weight(256, 512, seed=32, dtype=wdtype)
+    b = torch.randn(256, device="cuda")
+    ops.set_weight_cache(False)
+    try:
+        y0 = ops.spike_linear(S, weight=W, bias=b, branch="dense")
+    finally:
+        ops.set_weight_cache(True)
+    y1 = ops.spike_linear(S, weight=W, bias=b, branch="dense")
+    y2 = ops.spike_linear(S, weight=W, bias=b, branch="dense")  # cache hit
+    assert torch.equal(y0, y1) and torch.equal(y1, y2)
+    with torch.no_grad():
+        W.mul_(-0.5)
+    y3 = ops.spike_linear(S, weight=W, bias=b, branch="dense")
+    ops.set_weight_cache(False)
+    try:
+        y4 = ops.spike_linear(S, weight=W, bias=b, branch="dense")
+    finally:
+        ops.set_weight_cache(True)
+    assert torch.equal(y3, y4) and not torch.equal(y3, y1)
+    if wdtype == torch.float32:
+        x = torch.randn(900, 512, device="cuda")
+        a1 = ops.linear_act(x, W, b, act="heaviside")
+        ops.set_weight_cache(False)
+        try:
+            a0 = ops.linear_act(x, W, b, act="heaviside")
+        finally:
+            ops.set_weight_cache(True)
+        assert torch.equal(a0, a1)
+
+
+def test_prepared_weight_image_through_the_c_abi():
+    """spk_weight_image once, then spk_spike_linear_img twice: identical to
+    spk_spike_linear, which rebuilds the image itself."""
+    import ctypes
+
+    from spikestack_lite_b200 import _lib
+
+    lib = _lib.load()
+    T, M, K, N = 2, 513, 256, 192
+    S = _spikes(T, M, K, 0.2, seed=41)
+    WT = _weight(N, K, seed=42).t().contiguous()  # weightT [K, N]
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nb = lib.spk_weight_image_bytes(K, N, _lib.SPK_F32)
+    buf = torch.empty(nb + 1024, dtype=torch.uint8, device="cuda")
+    off = (-buf.data_ptr()) % 1024
+    img = buf[off:off + nb]
+    _lib.check(lib.spk_weight_image(WT.data_ptr(), _lib.SPK_F32, N, 1, K, N, img.data_ptr(), nb, stream),
+               "spk_weight_image")
+    wsn = lib.spk_spike_linear_workspace_bytes(T, M, K, N, _lib.SPK_F32)
+    ws = torch.empty(wsn, dtype=torch.uint8, device="cuda")
+    ys = []
+    for use_img in (False, True, True):
+        Y = torch.empty(T, M, N, device="cuda")
+        if use_img:
+            rc = lib.spk_spike_linear_img(S.data_ptr(), T, M, K, WT.data_ptr(), _lib.SPK_F32, N, 1, N, img.data_ptr(),
+                                          None, Y.data_ptr(), None, None, None, None, None, 0, _lib.BRANCH_DENSE,
+                                          ws.data_ptr(), wsn, stream)
+        else:
+            rc = lib.spk_spike_linear(S.data_ptr(), T, M, K, WT.data_ptr(), _lib.SPK_F32, N, 1, N, None, Y.data_ptr(),
+                                      None, None, None, None, None, 0, _lib.BRANCH_DENSE, ws.data_ptr(), wsn, stream)
+        _lib.check(rc, "spike_linear")
+        ys.append(Y)
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+    assert O.rel_err(ys[1].cpu().numpy(), O.spike_linear(S.cpu().numpy(), WT.cpu().numpy())) < TOL
