@@ -191,11 +191,27 @@ int spk_sparse_multistep_forward(const float* dense_input, int T, int64_t B, int
  * fp32-accurate on the tensor cores (tf32 hi/lo splits of W and X).  Needs
  * N > 64, K % 4 == 0 and a 16-byte aligned X.  Replaces the nn.Linear +
  * threshold + Heaviside pairs around the spike-linear path. */
-enum { SPK_ACT_NONE = 0, SPK_ACT_HEAVISIDE = 1, SPK_ACT_VSPIKE = 2 };
+enum { SPK_ACT_NONE = 0, SPK_ACT_HEAVISIDE = 1, SPK_ACT_VSPIKE = 2, SPK_ACT_HEAVISIDE_BITS = 3 };
+/* SPK_ACT_HEAVISIDE_BITS: the Heaviside spikes of SPK_ACT_HEAVISIDE packed one
+ * bit each, Y read as uint32 [R][N/32] (bit b of word w of a row = column
+ * 32w + b; N % 32 == 0): 32x fewer bytes than the fp32 spike tensor for the
+ * layer that consumes them (spk_spike_linear_bits).  Replaces the dense fp32
+ * act tensor of SpikingFFN (attention.py:156), which the reference writes
+ * and fc2 reads back. */
 size_t spk_linear_act_workspace_bytes(int K, int N);
 int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n, int N,
                    const float* bias, int act, float thr, float* Y, void* workspace, size_t workspace_bytes,
                    spk_stream_t stream);
+/* Spike-linear over packed spikes: bits [T*M][K/32] as written by
+ * SPK_ACT_HEAVISIDE_BITS (K % 64 == 0), fp32 W with strides as for
+ * spk_spike_linear (N > 64), Y [T, M, N] fp32 = S W (+ bias), bit-identical to
+ * spk_spike_linear's dense branch on the unpacked spikes.  w_image: optional,
+ * from spk_weight_image; the workspace (spk_linear_act_workspace_bytes(K, N)
+ * bytes) may be NULL with an image.  The fc2 of SpikingFFN
+ * (attention.py:158) on fc1's packed spikes. */
+int spk_spike_linear_bits(const uint32_t* bits, int T, int64_t M, int K, const float* W, int64_t w_stride_k,
+                          int64_t w_stride_n, int N, const void* w_image, const float* bias, float* Y,
+                          void* workspace, size_t workspace_bytes, spk_stream_t stream);
 /* spk_linear_act with a weight image prepared by spk_weight_image (fp32 W);
  * the workspace may then be NULL. */
 int spk_linear_act_img(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n,

@@ -44,6 +44,7 @@ SIGNATURES = {
     "spk_spike_linear_img": (_I, [_P, _I, _L, _I, _P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _L, _I, _P, _Z,
                                   _P]),
     "spk_linear_act_img": (_I, [_P, _L, _I, _P, _L, _L, _I, _P, _P, _I, _F, _P, _P, _Z, _P]),
+    "spk_spike_linear_bits": (_I, [_P, _I, _L, _I, _P, _L, _L, _I, _P, _P, _P, _P, _Z, _P]),
     "spk_sparse_forward_workspace_bytes": (_Z, [_I, _L, _I, _I]),
     "spk_sparse_forward": (_I, [_P, _L, _I, _P, _I, _P, _P, _P, _P, _L, _P, _I, _P, _Z, _P]),
     "spk_sparse_multistep_forward": (_I, [_P, _I, _L, _I, _P, _I, _P, _P, _P, _P, _L, _P, _I, _P, _Z, _P]),

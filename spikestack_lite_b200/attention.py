@@ -167,7 +167,19 @@ class SpikingFFN(nn.Module):
             self.fc2 = nn.Linear(d_model * expansion, d_model)
 
     def forward(self, x, record=None):
-        """``record`` (a dict, optional) receives the fc1 spikes ("act")."""
+        """``record`` (a dict, optional) receives the fc1 spikes ("act").
+
+        At inference on a temporal input with the SpikeSkip fc2, fc1's spikes
+        go to fc2 packed one bit each (ops.linear_act "heaviside_bits" ->
+        SparseLinear.forward_bits): the reference's dense fp32 act tensor
+        (attention.py:156) is never written."""
+        if (self.use_spikeskip and x.dim() == 4 and self.fc1.out_features % 64 == 0
+                and self.fc2.out_features > 64 and x.dtype == torch.float32):
+            bits = engine_linear(self.fc1, x, "heaviside_bits", self.threshold)
+            if bits is not None:
+                if record is not None:
+                    record["act"] = ops.unpack_spikes(bits, self.fc1.out_features)
+                return self.fc2.forward_bits(bits)
         act = engine_linear(self.fc1, x, "heaviside", self.threshold)
         if act is None:
             act = spike_fn(self.fc1(x) - self.threshold)

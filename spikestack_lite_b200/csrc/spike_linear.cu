@@ -400,7 +400,8 @@ static int linear_act_impl(const float* X, int64_t R, int K, const float* W, int
   SPK_REQUIRE(R >= 0 && K >= 1 && N >= 1, "bad shape R=%lld K=%d N=%d", (long long)R, K, N);
   SPK_REQUIRE(R < (int64_t(1) << 31), "linear_act: at most 2^31 - 1 rows per call (TMA row coordinates)");
   SPK_REQUIRE(W && (R == 0 || (X && Y)), "X, W and Y must be non-null");
-  SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_VSPIKE, "unknown activation %d", act);
+  SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_HEAVISIDE_BITS, "unknown activation %d", act);
+  SPK_REQUIRE(act != SPK_ACT_HEAVISIDE_BITS || N % 32 == 0, "packed spikes need N %% 32 == 0 (N=%d)", N);
   SPK_REQUIRE(N > 64, "linear_act needs N > 64 (128-column tiles on the tensor cores)");
   SPK_REQUIRE(K % 4 == 0 && (R == 0 || tc_supported(K, N, X)), "linear_act needs K %% 4 == 0 and a 16-byte aligned X");
   const TcPlan p = tc_plan(K, N, SPK_F32);
@@ -419,4 +420,35 @@ static int linear_act_impl(const float* X, int64_t R, int K, const float* W, int
   TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
   o.early_s = w_image == nullptr ? 1 : 0;
   return launch_wt(X, R, K, N, p, img, o, st, act, thr);
+}
+
+extern "C" int spk_spike_linear_bits(const uint32_t* bits, int T, int64_t M, int K, const float* W, int64_t w_stride_k,
+                                     int64_t w_stride_n, int N, const void* w_image, const float* bias, float* Y,
+                                     void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  using namespace spk;
+  SPK_REQUIRE(T >= 1 && M >= 0 && K >= 1 && N >= 1, "bad shape T=%d M=%lld K=%d N=%d", T, (long long)M, K, N);
+  const int64_t R = (int64_t)T * M;
+  SPK_REQUIRE(R < (int64_t(1) << 31), "packed spike-linear: at most 2^31 - 1 rows per call");
+  SPK_REQUIRE(W && (R == 0 || (bits && Y)), "bits, W and Y must be non-null");
+  SPK_REQUIRE(K % 64 == 0, "packed spikes need K %% 64 == 0 (K=%d)", K);
+  SPK_REQUIRE(N > 64, "packed spike-linear needs N > 64 (128-column tiles on the tensor cores)");
+  SPK_REQUIRE((reinterpret_cast<uintptr_t>(bits) & 3) == 0, "bits must be 4-byte aligned");
+  SPK_REQUIRE(w_image == nullptr || (reinterpret_cast<uintptr_t>(w_image) & 1023) == 0,
+              "the weight image must be 1024-byte aligned");
+  const TcPlan p = tc_plan(K, N, SPK_F32);
+  const size_t need = align_up(tf32_img_bytes(p), 1024);
+  if (w_image == nullptr && (workspace == nullptr || workspace_bytes < need))
+    return fail(SPK_EWORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  if (R == 0) return SPK_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned char* img = static_cast<const unsigned char*>(w_image);
+  if (img == nullptr) {
+    unsigned char* wimg = static_cast<unsigned char*>(workspace);
+    int rc = launch_w_image_tf32(W, w_stride_k, w_stride_n, K, N, p, wimg, nullptr, 0, st);
+    if (rc) return rc;
+    img = wimg;
+  }
+  TcOut o{bias, Y, nullptr, nullptr, nullptr, nullptr, nullptr};
+  o.early_s = w_image == nullptr ? 1 : 0;
+  return launch_wt_bits(bits, R, K, N, p, img, o, st);
 }

@@ -87,6 +87,7 @@ struct TcArgs {
   unsigned long long* sup_sum;  // spikes per 16384-row super-block
   float thr;              // threshold of the spiking epilogues of the linear-activation op
   const int* gate;        // automatic branch choice: run only when *gate == SPK_BRANCH_DENSE (null: always)
+  const uint32_t* bits_in;  // packed spikes [R][K/32] (the weights-in-TMEM kernel's packed input), or null
   int early_s;            // 1: the weight-image kernel (a plain launch) directly precedes this programmatic
                           // dependent, so S is complete and may be read before griddepcontrol.wait
 };

@@ -85,7 +85,8 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
 enum WtEpilogue : int {
   kEpiLinear = 0,     // y
   kEpiHeaviside = 1,  // 1 if y - thr > 0 else 0 (spike_fn(fc1(x) - thr); q, k spikes with thr = 0)
-  kEpiVSpike = 2      // 1 if (tanh(y) + 1) / 2 - thr > 0 else 0 (the v spikes, thr = tau)
+  kEpiVSpike = 2,     // 1 if (tanh(y) + 1) / 2 - thr > 0 else 0 (the v spikes, thr = tau)
+  kEpiHeavisideBits = 3  // the Heaviside spikes packed: bit b of word w of a row = column 32w + b
 };
 
 template <int kEpi>
@@ -152,8 +153,56 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
   }
 }
 
+// Converter warps of the packed-spike input (kBits).  The spikes arrive as
+// 32-bit words, bit b of word w of a row = column 32w + b; each slot (128
+// rows x 64 columns = two words per row) is expanded into fp32 0 / 1 in the
+// K-major 128-byte swizzle of the B operand, exactly the values a TMA load of
+// the unpacked spikes would have put there.  Warp cw fills rows 8cw..8cw+7;
+// lane l takes row 8cw + l/4 and columns 16(l%4) .. +15 (four 16-byte
+// chunks).  The slot is free again when the MMAs that read it committed
+// (stg_empty), and ready for them when every converter arrived on chk.
+template <int NS, int G>
+__device__ __forceinline__ void bits_converter(const int cw, const int lane, unsigned char* stg, uint64_t* chk,
+                                               uint64_t* stg_empty, uint8_t* lo_flag, volatile int* abort_flag,
+                                               const uint32_t* bits, const int KW, const int64_t r_begin,
+                                               const int64_t r_end, const int nk, const int groups, const int tiles) {
+  constexpr int CW = wt::kConvWarps;
+  const int rl = cw * (wt::kRows / CW) + (lane >> 2);  // row within the tile
+  const int q = lane & 3;                               // 16-column group of the slot
+  const uint32_t abase = (uint32_t)((q >> 1) * wt::kAtomBytes);
+  int j = 0;
+  bool ok = true;
+  for (int g = 0; g < groups && ok; ++g) {
+    const int tg = min(G, tiles - g * G);
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      for (int t = 0; t < tg; ++t, ++j) {
+        const int s = j % NS;
+        if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        const int64_t row = r_begin + (int64_t)(g * G + t) * wt::kRows + rl;
+        const uint32_t w = row < r_end ? bits[row * KW + 2 * kc + (q >> 1)] : 0u;
+        const uint32_t h = (w >> ((q & 1) * 16)) & 0xffffu;
+        unsigned char* st = stg + s * wt::kStgBytes;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const uint32_t nib = h >> (4 * c4);
+          const float4 f = make_float4((nib & 1u) ? 1.0f : 0.0f, (nib & 2u) ? 1.0f : 0.0f, (nib & 4u) ? 1.0f : 0.0f,
+                                       (nib & 8u) ? 1.0f : 0.0f);
+          *reinterpret_cast<float4*>(st + abase + sw128_chunk((uint32_t)rl, (uint32_t)((q & 1) * 4 + c4))) = f;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          lo_flag[s * CW + cw] = 0;  // exact: no lo pass
+          mbar_arrive(&chk[s]);
+        }
+      }
+    }
+  }
+}
+
 // kRelu: spike-linear (relu'(S)); false: the linear-activation op (plain X).
-template <int kEpi, bool kRelu>
+// kBits (with kRelu): the spikes come packed, 1 bit each (a.bits_in).
+template <int kEpi, bool kRelu, bool kBits = false>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
   if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
@@ -198,7 +247,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(&stg_full[s], 1);
       mbar_init(&chk[s], CW);
-      mbar_init(&stg_empty[s], CW + 1);
+      mbar_init(&stg_empty[s], kBits ? 1 : CW + 1);  // packed spikes: the MMAs' commit only
       mbar_init(&lo_go[s], 1);
       mbar_init(&lo_full[s], CW);
     }
@@ -240,7 +289,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- S producer
-    if (lane == 0) {
+    // (none for packed spikes: the converter warps build the slots)
+    if (lane == 0 && !kBits) {
       tma_prefetch_map(&tmap_s);
       auto load_s = [&](int s, int64_t row0, int kc) {
         // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
@@ -388,6 +438,9 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     if constexpr (!kRelu) {
       linear_converter<NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, abort_flag, r_begin, r_end,
                                   nk, groups, tiles);
+    } else if constexpr (kBits) {
+      bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, lo_flag, abort_flag, a.bits_in, a.K / 32, r_begin,
+                            r_end, nk, groups, tiles);
     } else {
       tf32_converter<NS, G, kRelu>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count,
                                    abort_flag, a, r_begin, r_end, n_tile, nk, groups, tiles);
@@ -449,7 +502,21 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           tmem_ld16(tmem + lane_base + wt::kDcol + (uint32_t)(t * wt::kRows + rb), v);
           tmem_wait_ld();
           tmem_reg_fence(v);
-          if (n < a.N) {
+          if constexpr (kEpi == kEpiHeavisideBits) {
+            // one ballot per row gives the row's word of this warp's 32 columns (N % 32 == 0:
+            // a warp's columns are all in range or all out); lane jj stores row rb + jj's word
+            if (n0 + q * 32 < a.N) {
+              uint32_t word = 0u;
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const uint32_t b = __ballot_sync(0xffffffffu, v[jj] + bias_n - a.thr > 0.0f);
+                if (lane == jj) word = b;
+              }
+              const int NW = a.N / 32;
+              if (lane < 16 && row0 + rb + lane < r_end)
+                reinterpret_cast<uint32_t*>(a.Y)[(row0 + rb + lane) * NW + (n0 / 32 + q)] = word;
+            }
+          } else if (n < a.N) {
             float* y = a.Y + (row0 + rb) * a.N + n;
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj)
@@ -475,9 +542,9 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 // The weight image is the tf32 kernel's (tf32_img_bytes, w_image_tf32_kernel)
 // with NT = 128: per N tile and K chunk the pieces hi k0-31 | hi k32-63 |
 // lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle.
-template <int kEpi, bool kRelu>
+template <int kEpi, bool kRelu, bool kBits = false>
 int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
-  auto kern = spike_linear_wt_kernel<kEpi, kRelu>;
+  auto kern = spike_linear_wt_kernel<kEpi, kRelu, kBits>;
   constexpr size_t smem = wt::Ring<kRelu>::kSmemBytes;
   SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t gx = ceil_div(a.R, a.rows_per_cta);
@@ -490,14 +557,7 @@ int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStr
   return SPK_OK;
 }
 
-// act < 0: spike-linear (relu'(S) with the CSR outputs of `o`); act >= 0: the
-// linear-activation op with epilogue `act` (WtEpilogue) and threshold `thr`.
-int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
-              cudaStream_t stream, int act = -1, float thr = 0.0f) {
-  if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
-  CUtensorMap map;
-  int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
-  if (rc) return rc;
+inline TcArgs wt_args(int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o, float thr) {
   TcArgs a{};
   a.R = R;
   a.K = K;
@@ -519,14 +579,41 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   const int sms = sm_count();
   const int ranges = sms / p.n_tiles > 0 ? sms / p.n_tiles : 1;
   a.rows_per_cta = ceil_div(ceil_div(a.R, ranges), 32) * 32;
+  return a;
+}
+
+// act < 0: spike-linear (relu'(S) with the CSR outputs of `o`); act >= 0: the
+// linear-activation op with epilogue `act` (WtEpilogue) and threshold `thr`;
+// kEpiHeavisideBits writes the spikes packed into o.Y as uint32 [R][N/32].
+int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
+              cudaStream_t stream, int act = -1, float thr = 0.0f) {
+  if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
+  if (act == kEpiHeavisideBits && N % 32 != 0) return fail(SPK_EINVAL, "packed spikes need N %% 32 == 0 (N=%d)", N);
+  CUtensorMap map;
+  int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
+  if (rc) return rc;
+  const TcArgs a = wt_args(R, K, N, p, img, o, thr);
   switch (act) {
     case -1: return launch_wt_inst<kEpiLinear, true>(map, a, p.n_tiles, stream);
     case kEpiLinear: return launch_wt_inst<kEpiLinear, false>(map, a, p.n_tiles, stream);
     case kEpiHeaviside: return launch_wt_inst<kEpiHeaviside, false>(map, a, p.n_tiles, stream);
     case kEpiVSpike: return launch_wt_inst<kEpiVSpike, false>(map, a, p.n_tiles, stream);
+    case kEpiHeavisideBits: return launch_wt_inst<kEpiHeavisideBits, false>(map, a, p.n_tiles, stream);
     default: break;
   }
   return fail(SPK_EINVAL, "unknown activation %d", act);
+}
+
+// Spike-linear over packed spikes bits [R][K/32] (K % 64 == 0): Y = S W (+ bias), fp32 W.
+int launch_wt_bits(const uint32_t* bits, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img,
+                   const TcOut& o, cudaStream_t stream) {
+  if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
+  if (K % 64 != 0) return fail(SPK_EINVAL, "packed spikes need K %% 64 == 0 (K=%d)", K);
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));  // no tensor map: the converters read the words themselves
+  TcArgs a = wt_args(R, K, N, p, img, o, 0.0f);
+  a.bits_in = bits;
+  return launch_wt_inst<kEpiLinear, true, true>(map, a, p.n_tiles, stream);
 }
 
 }  // namespace spk

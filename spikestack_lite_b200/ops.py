@@ -183,7 +183,7 @@ def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=Non
     return Y[0] if squeeze else Y
 
 
-_ACTS = {"none": 0, "heaviside": 1, "vspike": 2}
+_ACTS = {"none": 0, "heaviside": 1, "vspike": 2, "heaviside_bits": 3}
 
 
 def linear_act(x, weight, bias=None, act="none", thr=0.0):
@@ -193,6 +193,8 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
       "none"       y
       "heaviside"  (y - thr > 0).float()               spike_fn(fc1(x) - thr); q, k spikes (thr 0)
       "vspike"     ((tanh(y) + 1) / 2 - thr > 0).float()  v spikes (thr = tau)
+      "heaviside_bits"  the "heaviside" spikes packed 32 to an int32 word:
+                   [..., N/32], bit b of word w = column 32w + b (N % 32 == 0)
 
     Needs N > 64 and K % 4 == 0."""
     require_cuda(x, weight, bias, what="linear_act")
@@ -209,7 +211,12 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
         if bias.numel() != N:
             raise EngineError("linear_act: bias must have N elements")
     R = x.numel() // K if K else 0
-    Y = torch.empty(*x.shape[:-1], N, dtype=torch.float32, device=x.device)
+    if act == "heaviside_bits":
+        if N % 32:
+            raise EngineError(f"linear_act: packed spikes need N % 32 == 0 (N={N})")
+        Y = torch.empty(*x.shape[:-1], N // 32, dtype=torch.int32, device=x.device)
+    else:
+        Y = torch.empty(*x.shape[:-1], N, dtype=torch.float32, device=x.device)
     lib = _lib.load()
     ws, wsn = _lib.workspace(x.device, lib.spk_linear_act_workspace_bytes(K, N))
     _record("linear_act", R, K, N)
@@ -227,6 +234,43 @@ def engine_linear(lin, x, act="none", thr=0.0):
     if torch.is_grad_enabled() or not x.is_cuda or lin.out_features <= 64 or lin.in_features % 4:
         return None
     return linear_act(x, lin.weight, lin.bias, act, thr)
+
+
+def spike_linear_bits(bits, K, weight, bias=None):
+    """Spike-linear over packed spikes: bits int32 [..., K/32] (bit b of word w
+    = column 32w + b, as linear_act(act="heaviside_bits") writes them), an
+    nn.Linear weight [N, K] fp32, optional bias -> [..., N] fp32; the same
+    values as spike_linear(unpack_spikes(bits, K), weight, bias,
+    branch="dense").  Needs K % 64 == 0 and N > 64."""
+    require_cuda(bits, weight, bias, what="spike_linear_bits")
+    require_f32(weight, bias, what="spike_linear_bits")
+    if bits.dtype != torch.int32:
+        raise EngineError(f"spike_linear_bits: bits must be int32, got {bits.dtype}")
+    bits = _contig(bits)
+    N, Kw = weight.shape
+    if Kw != K or bits.shape[-1] * 32 != K:
+        raise EngineError(f"spike_linear_bits: K={K}, weight K={Kw}, bits hold {bits.shape[-1] * 32} columns")
+    if bias is not None:
+        bias = _contig(bias)
+        if bias.numel() != N:
+            raise EngineError("spike_linear_bits: bias must have N elements")
+    R = bits.numel() // bits.shape[-1]
+    Y = torch.empty(*bits.shape[:-1], N, dtype=torch.float32, device=bits.device)
+    lib = _lib.load()
+    _record("spike_linear", R, K, N)
+    img = _weight_image(weight, K, N, weight.stride(1), weight.stride(0), _lib.SPK_F32)
+    ws, wsn = (None, 0) if img is not None else _lib.workspace(bits.device, lib.spk_linear_act_workspace_bytes(K, N))
+    check(lib.spk_spike_linear_bits(ptr(bits), 1, R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(img),
+                                    ptr(bias), ptr(Y), ws, wsn, stream_of(bits)), "spk_spike_linear_bits")
+    return Y
+
+
+def unpack_spikes(bits, K):
+    """fp32 0 / 1 spikes [..., K] from packed words [..., K/32] (inspection and
+    tests; the engine consumes the packed form directly)."""
+    shifts = torch.arange(32, device=bits.device, dtype=torch.int32)
+    b = (bits.unsqueeze(-1) >> shifts) & 1
+    return b.reshape(*bits.shape[:-1], bits.shape[-1] * 32)[..., :K].float()
 
 
 def alloc_csr(T, M, K, device, capacity=None, values=False):

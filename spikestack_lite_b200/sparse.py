@@ -140,6 +140,13 @@ class SparseLinear(torch.nn.Module):
         self.csr = csr
         return out.view(T, *leading, self.out_features)
 
+    def forward_bits(self, bits):
+        """(*, in_features / 32) int32 packed spikes (bit b of word w = input
+        column 32w + b) -> (*, out_features), on the engine's dense branch,
+        inference only: the fc2 of SpikingFFN on fc1's packed spikes."""
+        self._check(bits)
+        return ops.spike_linear_bits(bits, self.in_features, self.linear.weight, self.linear.bias)
+
     def forward(self, x):
         """Density-dispatched forward (sparse/__init__.py:264-280): the
         spike-linear engine for wide layers (in_features >= sparse_threshold) at

@@ -100,3 +100,37 @@ def test_rejects_unsupported():
         ops.linear_act(x.cpu(), w.cpu(), None)                    # no CPU path
     with pytest.raises(EngineError):
         ops.linear_act(x, w, b, act="relu")
+
+
+@pytest.mark.parametrize("R,K,N", [(1000, 512, 2048), (4097, 64, 96), (300, 256, 160)])
+def test_heaviside_bits_pack_the_heaviside_spikes(R, K, N):
+    """act="heaviside_bits" writes the same decisions as "heaviside", packed one
+    bit each (bit b of word w = column 32w + b), partial row tiles included."""
+    g = torch.Generator(device="cuda").manual_seed(R + N)
+    x = torch.randn(R, K, generator=g, device="cuda")
+    w = torch.randn(N, K, generator=g, device="cuda") / K ** 0.5
+    b = torch.randn(N, generator=g, device="cuda") * 0.1
+    spikes = ops.linear_act(x, w, b, act="heaviside", thr=0.05)
+    bits = ops.linear_act(x, w, b, act="heaviside_bits", thr=0.05)
+    assert bits.dtype == torch.int32 and bits.shape == (R, N // 32)
+    assert torch.equal(ops.unpack_spikes(bits, N), spikes)
+
+
+@pytest.mark.parametrize("T,M,K,N", [(4, 1000, 2048, 512), (2, 4097, 128, 96), (1, 129, 64, 200)])
+def test_spike_linear_bits_matches_the_unpacked_dense_branch(T, M, K, N):
+    """fc2 on packed spikes gives bit-identical output to the dense branch on
+    the unpacked fp32 spikes (the expanded staging slots hold the same values
+    a TMA load of them would)."""
+    g = torch.Generator(device="cuda").manual_seed(T * M + K)
+    S = (torch.rand(T, M, K, generator=g, device="cuda") < 0.5).float()
+    shifts = torch.arange(32, device="cuda", dtype=torch.int64)
+    words = (S.view(T, M, K // 32, 32).long() << shifts).sum(-1)
+    bits = torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+    assert torch.equal(ops.unpack_spikes(bits, K), S)
+    w = torch.randn(N, K, generator=g, device="cuda") / K ** 0.5
+    b = torch.randn(N, generator=g, device="cuda")
+    y_bits = ops.spike_linear_bits(bits, K, w, b)
+    y_dense = ops.spike_linear(S, weight=w, bias=b, branch="dense")
+    assert torch.equal(y_bits, y_dense)
+    ref = S.cpu().double() @ w.cpu().double().t() + b.cpu().double()
+    assert float((y_bits.cpu().double() - ref).abs().max() / ref.abs().max()) < 1e-4
