@@ -857,6 +857,43 @@ def run_crossover(args, dist, cfg):
             "peak_bf16_tflops": pk["bf16_tflops"], "crossover": table}
 
 
+def run_gsmc(args, dist, cfg):
+    """The GSMC recurrence at the model's chunk geometry (M = 64 samples x
+    1024 tokens, d = 512, T = 4): the two-kernel form (gr through the
+    spike-linear dense branch, then the step kernel) against the fused form
+    (one kernel per plane, gates in the epilogue), CUDA events."""
+    from spikestack_lite_b200 import ops
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    T, M, d = cfg["T"], cfg["M"], cfg["d"]
+    g = torch.Generator(device=dev).manual_seed(5)
+    gi = torch.randn(T, M, 4 * d, generator=g, device=dev) * 2.0
+    wd = torch.randn(T, M, d, generator=g, device=dev) * 0.5
+    w_rec = torch.randn(4 * d, d, generator=g, device=dev) * (0.5 / d ** 0.5)
+    bias = torch.randn(4 * d, generator=g, device=dev)
+    res = {}
+    outs = {}
+    for form in ("two_kernel", "fused"):
+        f = form == "fused"
+        for _ in range(args.warmup):
+            ops.gsmc_forward(gi, wd, w_rec, bias, fused=f)
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            outs[form] = ops.gsmc_forward(gi, wd, w_rec, bias, fused=f)
+        stop.record()
+        torch.cuda.synchronize()
+        res[form + "_ms"] = round(dist.max(start.elapsed_time(stop)) / args.steps, 4)
+    same = bool(torch.equal(outs["two_kernel"], outs["fused"]))
+    return {"metric": METRIC, "value": res["two_kernel_ms"], "unit": "ms", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "T": T, "M": M, "d": d}, **res,
+            "fused_equals_two_kernel": same,
+            "gr_bytes_not_written_per_plane": 2 * 4 * M * 4 * d}
+
+
 def run_reference_model(args, dist, cfg):
     """--impl reference for the model: the reference's CPU forward (restated in
     oracle/, the reference's own PyTorch CPU arithmetic) on a sample of the
@@ -891,6 +928,8 @@ WORKLOADS = {
     "crossover": {"name": "spike-linear density sweep S[4,65536,2048], W[2048,2048] bf16: dense vs CSR vs auto",
                   "T": 4, "M": 65536, "K": 2048, "N": 2048,
                   "densities": [0.01, 0.02, 0.05, 0.1, 0.2, 0.35, 0.5]},
+    "gsmc": {"name": "GSMC recurrence at the model's chunk geometry: M = 65536, d = 512, T = 4", "T": 4,
+             "M": 65536, "d": 512},
     "linear": {"name": "C5 SpikingFFN fc1 + threshold spike: x[4*512*1024, 512] -> [.., 2048]", "R": 4 * 512 * 1024,
                "rows_per_batch": 4 * 1024, "K": 512, "N": 2048, "thr": 0.0},
     "attention": {"name": "spiking linear attention B=64 H=8 L=4096 dh=64 T=4 p=0.15", "T": 4, "B": 64,
@@ -960,6 +999,8 @@ def main():
     try:
         if args.workload in ("spike_linear", "sweep"):
             res = run_spike_linear(args, dist, cfg)
+        elif args.workload == "gsmc":
+            res = run_gsmc(args, dist, cfg)
         elif args.workload == "crossover":
             res = run_crossover(args, dist, cfg)
         elif args.workload == "attention":

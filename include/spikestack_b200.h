@@ -252,6 +252,18 @@ int spk_gsmc_step(const float* gi, const float* gr, const float* wd, const float
  * cell step.  out_all [T, M, d] (optional) receives every step's spikes and
  * pooled [M, d] their mean over T (pool_mean != 0) or the last step. */
 size_t spk_gsmc_workspace_bytes(int64_t M, int d);
+/* Forms of the recurrence for spk_gsmc_forward_ex.  SPK_GSMC_TWO_KERNEL (the
+ * default of spk_gsmc_forward): per plane gr = W_rec s_{t-1} through the
+ * spike-linear dense branch, then the step kernel.  SPK_GSMC_FUSED: one
+ * tensor-core kernel per plane with the gates, state update and pooling in
+ * its epilogue (gr stays on chip; d % 32 == 0, else the two-kernel form);
+ * bit-identical results.  No counterpart in the reference (its loop,
+ * gsmc.py:119-142, runs W_rec then fused_gsmc_step). */
+enum { SPK_GSMC_TWO_KERNEL = 0, SPK_GSMC_FUSED = 1 };
+int spk_gsmc_forward_ex(const float* gi_all, const float* wd_all, const float* w_rec, const float* bias, int T,
+                        int64_t M, int d, float v_th, float gate_scale, int adaptive, float beta, int pool_mean,
+                        float* out_all, float* pooled, void* workspace, size_t workspace_bytes, int form,
+                        spk_stream_t stream);
 int spk_gsmc_forward(const float* gi_all, const float* wd_all, const float* w_rec, const float* bias, int T,
                      int64_t M, int d, float v_th, float gate_scale, int adaptive, float beta, int pool_mean,
                      float* out_all, float* pooled, void* workspace, size_t workspace_bytes, spk_stream_t stream);

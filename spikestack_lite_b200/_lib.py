@@ -55,6 +55,7 @@ SIGNATURES = {
     "spk_gsmc_step": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _L, _I, _F, _F, _I, _F, _P]),
     "spk_gsmc_workspace_bytes": (_Z, [_L, _I]),
     "spk_gsmc_forward": (_I, [_P, _P, _P, _P, _I, _L, _I, _F, _F, _I, _F, _I, _P, _P, _P, _Z, _P]),
+    "spk_gsmc_forward_ex": (_I, [_P, _P, _P, _P, _I, _L, _I, _F, _F, _I, _F, _I, _P, _P, _P, _Z, _I, _P]),
     "spk_add_layernorm": (_I, [_P, _P, _P, _P, _L, _I, _F, _P, _P, _P]),
     "spk_selftest_wait_timeout": (_I, [_P]),
     "spk_spire_planes": (_I, [_P, _P, _P, _P, _I, _L, _I, _I, _P, _P]),

@@ -88,6 +88,7 @@ struct TcArgs {
   float thr;              // threshold of the spiking epilogues of the linear-activation op
   const int* gate;        // automatic branch choice: run only when *gate == SPK_BRANCH_DENSE (null: always)
   const uint32_t* bits_in;  // packed spikes [R][K/32] (the weights-in-TMEM kernel's packed input), or null
+  GsmcCell cell;          // the GSMC recurrence's epilogue (weights-in-TMEM kernel, kEpiGsmc)
   int early_s;            // 1: the weight-image kernel (a plain launch) directly precedes this programmatic
                           // dependent, so S is complete and may be read before griddepcontrol.wait
 };

@@ -53,13 +53,17 @@ constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 col
 constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
 // Shared-memory rings per mode.  Spike-linear: five S slots.  Linear op:
 // three X slots and two remainder buffers (the X slot itself is the hi part).
-template <bool kRelu>
+// The GSMC recurrence (kXchg) gives one S slot to the epilogue's 16 KB gate
+// exchange buffer.
+template <bool kRelu, bool kXchg = false>
 struct Ring {
-  static constexpr int NS = kRelu ? 5 : 3;  // staging slots
+  static constexpr int NS = kRelu ? (kXchg ? 4 : 5) : 3;  // staging slots
   static constexpr int NL = kRelu ? 0 : 2;  // remainder buffers
-  static constexpr size_t kRing = (size_t)(NS + NL) * kStgBytes + (size_t)kNP * kPieceBytes;
+  static constexpr size_t kXchgBytes = kXchg ? 2 * 4 * 16 * 32 * sizeof(float) : 0;  // [2][4 gates][16 rows][32]
+  static constexpr size_t kRing = (size_t)(NS + NL) * kStgBytes + (size_t)kNP * kPieceBytes + kXchgBytes;
   // barriers, lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
-  static constexpr int kBars = 5 * NS + 2 * NL + 2 * kNP + 7;
+  static constexpr int kBarsUsed = 5 * NS + 2 * NL + 2 * kNP + 7;
+  static constexpr int kBars = kBarsUsed + (kBarsUsed & 1);  // even: the lo flags after them stay 16-byte aligned
   static constexpr size_t kTail = 8 * kBars + kConvWarps * NS + 4 * kRows * kG + 16;
   static constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
   static_assert((8 * kBars) % 16 == 0, "lo flags 16-byte aligned");
@@ -86,7 +90,8 @@ enum WtEpilogue : int {
   kEpiLinear = 0,     // y
   kEpiHeaviside = 1,  // 1 if y - thr > 0 else 0 (spike_fn(fc1(x) - thr); q, k spikes with thr = 0)
   kEpiVSpike = 2,     // 1 if (tanh(y) + 1) / 2 - thr > 0 else 0 (the v spikes, thr = tau)
-  kEpiHeavisideBits = 3  // the Heaviside spikes packed: bit b of word w of a row = column 32w + b
+  kEpiHeavisideBits = 3,  // the Heaviside spikes packed: bit b of word w of a row = column 32w + b
+  kEpiGsmc = 4            // the GSMC cell update from the recurrent gate projections (a.cell)
 };
 
 template <int kEpi>
@@ -206,14 +211,15 @@ template <int kEpi, bool kRelu, bool kBits = false>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
   if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
-  using RG = wt::Ring<kRelu>;
+  using RG = wt::Ring<kRelu, kEpi == kEpiGsmc>;
   constexpr int G = wt::kG, NS = RG::NS, NL = RG::NL, NP = wt::kNP, CW = wt::kConvWarps;
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
   unsigned char* lob = stg + NS * wt::kStgBytes;              // [NL][32 KB] remainders (linear op)
   unsigned char* pcs = lob + NL * wt::kStgBytes;              // [NP][16 KB] weight pieces
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes);
+  float* xbuf = reinterpret_cast<float*>(pcs + NP * wt::kPieceBytes);  // GSMC gate exchange (kXchgBytes)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes + RG::kXchgBytes);
   uint64_t* stg_full = bars;
   uint64_t* chk = stg_full + NS;
   uint64_t* stg_empty = chk + NS;
@@ -228,7 +234,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* drain = acc_empty + 1;
   uint64_t* lof = drain + 1;   // [NL] remainder buffer written (linear op)
   uint64_t* loe = lof + NL;    // [NL] remainder buffer read by the MMAs
-  static_assert(5 * NS + 2 * NP + 7 + 2 * NL == RG::kBars, "the barriers above fill the barrier block");
+  static_assert(5 * NS + 2 * NP + 7 + 2 * NL == RG::kBarsUsed, "the barriers above fill the barrier block");
   uint8_t* lo_flag = reinterpret_cast<uint8_t*>(bars + RG::kBars);  // [NS][CW] bytes, 16-byte aligned
   int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
@@ -498,11 +504,36 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 #pragma unroll 1
         for (int rb = 0; rb < wt::kRows; rb += 16) {
           if (row0 + rb >= r_end) break;
+          GsmcIn cin[4];  // GSMC: the inputs of this warp's 4 rows, requested before the accumulators are read
+          if constexpr (kEpi == kEpiGsmc) {
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+              const int64_t row = row0 + rb + q * 4 + r4;
+              if (row < r_end) cin[r4] = gsmc_load(a.cell, row, n_tile * 32 + lane);
+            }
+          }
           float v[16];
           tmem_ld16(tmem + lane_base + wt::kDcol + (uint32_t)(t * wt::kRows + rb), v);
           tmem_wait_ld();
           tmem_reg_fence(v);
-          if constexpr (kEpi == kEpiHeavisideBits) {
+          if constexpr (kEpi == kEpiGsmc) {
+            // The tile's 128 columns are the f, i, o, g projections (lane quarters 0-3) of the
+            // 32 channels 32 * n_tile + lane.  Each warp publishes its gate for 16 rows, then
+            // updates the cells of 4 of those rows for the 32 channels (all four gates at hand).
+            float* xb = xbuf + ((rb >> 4) & 1) * (4 * 16 * 32);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) xb[(q * 16 + jj) * 32 + lane] = v[jj];
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+            const int ch = n_tile * 32 + lane;
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+              const int rr = q * 4 + r4;
+              const int64_t row = row0 + rb + rr;
+              if (row < r_end)
+                gsmc_update(a.cell, row, ch, cin[r4], xb[(0 * 16 + rr) * 32 + lane], xb[(1 * 16 + rr) * 32 + lane],
+                            xb[(2 * 16 + rr) * 32 + lane], xb[(3 * 16 + rr) * 32 + lane]);
+            }
+          } else if constexpr (kEpi == kEpiHeavisideBits) {
             // one ballot per row gives the row's word of this warp's 32 columns (N % 32 == 0:
             // a warp's columns are all in range or all out); lane jj stores row rb + jj's word
             if (n0 + q * 32 < a.N) {
@@ -545,7 +576,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 template <int kEpi, bool kRelu, bool kBits = false>
 int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
   auto kern = spike_linear_wt_kernel<kEpi, kRelu, kBits>;
-  constexpr size_t smem = wt::Ring<kRelu>::kSmemBytes;
+  constexpr size_t smem = wt::Ring<kRelu, kEpi == kEpiGsmc>::kSmemBytes;
   SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t gx = ceil_div(a.R, a.rows_per_cta);
   dim3 grid((unsigned)gx, (unsigned)n_tiles);
@@ -602,6 +633,24 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
     default: break;
   }
   return fail(SPK_EINVAL, "unknown activation %d", act);
+}
+
+// One plane of the GSMC recurrence: the gate projections gr = s_prev W_rec^T
+// of the rows s_prev [R][K = d] on the tensor cores (img: the image of W_rec
+// with its rows permuted so that N tile c holds the f, i, o, g rows of the
+// channels 32c .. 32c+31) and the cell update in the epilogue; gr never
+// leaves the SM.
+int launch_wt_gsmc(const float* s_prev, int64_t R, int d, const TcPlan& p, const unsigned char* img,
+                   const GsmcCell& cell, cudaStream_t stream) {
+  if (p.NT != wt::kLanes || p.n_tiles * 32 != d) return fail(SPK_EINVAL, "GSMC recurrence: d %% 32 == 0 required");
+  CUtensorMap map;
+  int rc = make_map_2d_swizzled_f32(&map, s_prev, R, d, d, 32, wt::kBoxRows, "s");
+  if (rc) return rc;
+  TcOut o{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  o.early_s = 0;  // the previous plane's kernel writes s_prev
+  TcArgs a = wt_args(R, d, 4 * d, p, img, o, 0.0f);
+  a.cell = cell;
+  return launch_wt_inst<kEpiGsmc, true>(map, a, p.n_tiles, stream);
 }
 
 // Spike-linear over packed spikes bits [R][K/32] (K % 64 == 0): Y = S W (+ bias), fp32 W.

@@ -102,6 +102,84 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void report_device_error(int code) { atomicOr(&g_device_error, code); }
 
+// One GSMC cell update (FusedGSMC._step_gates / gsmc_step_kernel order,
+// gsmc_cuda.cu:11-77): pre = (gi + gr) / gate_scale + bias (the bias a second
+// time on top of the W_in bias inside gi), f, i, o = 1 / (1 + expf(-pre)),
+// g = tanhf(pre), a = f*m + i*g, v = o*tanhf(a) + wd, theta = v_th*(1 + heat)
+// (adaptive), s = v > theta, m = a - s*v_th, heat = beta*heat + s; and the
+// pooled output (mode 0: first plane of a mean, 1: middle, 2: last plane,
+// scaled, 3: "last" pooling, 4: mean over one plane).  Shared by the step
+// kernel and the fused recurrence so that both give the same bits.
+struct GsmcCell {
+  const float* gi;    // [M, 4d] this plane's input projection (with the W_in bias)
+  const float* wd;    // [M, d]
+  const float* bias;  // [4d] the W_in bias
+  float* m;           // [M, d] state, updated in place
+  float* heat;        // [M, d] state, updated in place
+  float* s_out;       // [M, d] this plane's spikes
+  float* out_t;       // [M, d] or null
+  float* pooled;      // [M, d] or null
+  int d;
+  float v_th, gate_scale, beta, pool_scale;
+  int adaptive, pool_mode;
+};
+
+__device__ __forceinline__ float gsmc_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// The cell's inputs, loaded ahead of its update (they do not depend on the
+// recurrent projection, so a caller can have them in flight meanwhile).
+struct GsmcIn {
+  float gi[4], wd, m, heat, pooled;
+};
+
+__device__ __forceinline__ GsmcIn gsmc_load(const GsmcCell& c, int64_t row, int col) {
+  const int d = c.d;
+  const int64_t idx = row * d + col;
+  const float* gir = c.gi + row * 4 * d;
+  GsmcIn in;
+  in.gi[0] = gir[col];
+  in.gi[1] = gir[d + col];
+  in.gi[2] = gir[2 * d + col];
+  in.gi[3] = gir[3 * d + col];
+  in.wd = c.wd[idx];
+  in.m = c.m[idx];
+  in.heat = c.heat[idx];
+  in.pooled = (c.pooled != nullptr && (c.pool_mode == 1 || c.pool_mode == 2)) ? c.pooled[idx] : 0.0f;
+  return in;
+}
+
+__device__ __forceinline__ void gsmc_update(const GsmcCell& c, int64_t row, int col, const GsmcIn& in, float gr_f,
+                                            float gr_i, float gr_o, float gr_g) {
+  const int d = c.d;
+  const int64_t idx = row * d + col;
+  const float f = gsmc_sigmoid((in.gi[0] + gr_f) / c.gate_scale + c.bias[col]);
+  const float i = gsmc_sigmoid((in.gi[1] + gr_i) / c.gate_scale + c.bias[d + col]);
+  const float o = gsmc_sigmoid((in.gi[2] + gr_o) / c.gate_scale + c.bias[2 * d + col]);
+  const float g = tanhf((in.gi[3] + gr_g) / c.gate_scale + c.bias[3 * d + col]);
+  const float a = f * in.m + i * g;
+  const float v = o * tanhf(a) + in.wd;
+  const float h = in.heat;
+  const float theta = c.adaptive ? c.v_th * (1.0f + h) : c.v_th;
+  const float sn = (v > theta) ? 1.0f : 0.0f;
+  c.m[idx] = a - sn * c.v_th;
+  c.s_out[idx] = sn;
+  c.heat[idx] = c.adaptive ? c.beta * h + sn : 0.0f;
+  if (c.out_t != nullptr) c.out_t[idx] = sn;
+  if (c.pooled != nullptr) {
+    float* p = c.pooled + idx;
+    if (c.pool_mode == 0) *p = sn;
+    else if (c.pool_mode == 1) *p = in.pooled + sn;
+    else if (c.pool_mode == 2) *p = (in.pooled + sn) * c.pool_scale;
+    else if (c.pool_mode == 3) *p = sn;
+    else *p = sn * c.pool_scale;
+  }
+}
+
+__device__ __forceinline__ void gsmc_cell(const GsmcCell& c, int64_t row, int col, float gr_f, float gr_i, float gr_o,
+                                          float gr_g) {
+  gsmc_update(c, row, col, gsmc_load(c, row, col), gr_f, gr_i, gr_o, gr_g);
+}
+
 // Device-side branch choice of spike-linear's automatic mode: a kernel given a
 // gate word runs only when the word holds its value (written by earlier
 // kernels of the same stream), otherwise it returns at once.

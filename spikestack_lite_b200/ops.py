@@ -433,10 +433,12 @@ def fused_gsmc_step(gi, gr, wd, bias, m, s, heat, v_th, gate_scale, adaptive_thr
 
 
 def gsmc_forward(gi_all, wd_all, w_rec, bias, v_th=1.0, gate_scale=4.0, adaptive=True, beta=0.8, pool="mean",
-                 return_planes=False):
+                 return_planes=False, fused=False):
     """The eval-mode GSMC recurrence (gsmc.py:96-148) over precomputed input
     projections gi_all [T, M, 4d] and wd_all [T, M, d]; w_rec is the W_rec
-    nn.Linear weight [4d, d].  Returns pooled [M, d] (and the planes [T, M, d])."""
+    nn.Linear weight [4d, d].  Returns pooled [M, d] (and the planes [T, M, d]).
+    fused=True: the recurrent projection and the cell update in one kernel per
+    plane (SPK_GSMC_FUSED; same results, slower at the model's geometry)."""
     require_cuda(gi_all, wd_all, w_rec, bias, what="gsmc_forward")
     require_f32(gi_all, wd_all, w_rec, bias, what="gsmc_forward")
     gi_all, wd_all, w_rec, bias = (_contig(t) for t in (gi_all, wd_all, w_rec, bias))
@@ -446,9 +448,10 @@ def gsmc_forward(gi_all, wd_all, w_rec, bias, v_th=1.0, gate_scale=4.0, adaptive
     lib = _lib.load()
     ws, wsn = _lib.workspace(gi_all.device, lib.spk_gsmc_workspace_bytes(M, d))
     _record("gsmc_recurrent", (T - 1) * M, d, 4 * d)  # W_rec s_{t-1} for t >= 1 (s_{-1} = 0 is skipped)
-    check(lib.spk_gsmc_forward(ptr(gi_all), ptr(wd_all), ptr(w_rec), ptr(bias), T, M, d, float(v_th),
-                               float(gate_scale), int(bool(adaptive)), float(beta), 1 if pool == "mean" else 0,
-                               ptr(planes), ptr(pooled), ws, wsn, stream_of(gi_all)), "spk_gsmc_forward")
+    check(lib.spk_gsmc_forward_ex(ptr(gi_all), ptr(wd_all), ptr(w_rec), ptr(bias), T, M, d, float(v_th),
+                                  float(gate_scale), int(bool(adaptive)), float(beta), 1 if pool == "mean" else 0,
+                                  ptr(planes), ptr(pooled), ws, wsn, 1 if fused else 0, stream_of(gi_all)),
+          "spk_gsmc_forward")
     return (pooled, planes) if return_planes else pooled
 
 

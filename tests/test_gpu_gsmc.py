@@ -73,3 +73,40 @@ def test_fused_recurrence_vs_oracle_engine_order():
     ref, _ = O.gsmc_forward(x.cpu(), sd, pool="mean", step="engine")
     frac = (np.abs(out.cpu().numpy() - ref.numpy()) > 1e-6).mean()
     assert frac < 1e-3
+
+
+@pytest.mark.parametrize("M,d,T,pool", [(4096, 512, 4, "mean"), (1000, 64, 3, "last"), (333, 96, 2, "mean")])
+def test_fused_recurrence_matches_the_two_kernel_form(M, d, T, pool):
+    """The fused recurrence (gate projections W_rec s_{t-1} in tensor memory,
+    cell update in the same kernel's epilogue) gives exactly the spikes and the
+    pooled output of the two-kernel form: gr through the spike-linear dense
+    branch, written out, then the step op."""
+    from spikestack_lite_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + d)
+    gi_all = torch.randn(T, M, 4 * d, generator=g, device="cuda") * 2.0
+    wd_all = torch.randn(T, M, d, generator=g, device="cuda") * 0.5
+    w_rec = torch.randn(4 * d, d, generator=g, device="cuda") * (0.5 / d ** 0.5)
+    bias = torch.randn(4 * d, generator=g, device="cuda")
+    pooled, planes = ops.gsmc_forward(gi_all, wd_all, w_rec, bias, pool=pool, return_planes=True, fused=True)
+    pooled2, planes2 = ops.gsmc_forward(gi_all, wd_all, w_rec, bias, pool=pool, return_planes=True)
+    assert torch.equal(planes, planes2) and torch.equal(pooled, pooled2)
+    m = torch.zeros(M, d, device="cuda")
+    s = torch.zeros(M, d, device="cuda")
+    heat = torch.zeros(M, d, device="cuda")
+    outs = []
+    for t in range(T):
+        gr = ops.spike_linear(s, weight=w_rec, branch="dense") if t > 0 else torch.zeros(M, 4 * d, device="cuda")
+        outs.append(ops.fused_gsmc_step(gi_all[t].contiguous(), gr, wd_all[t].contiguous(), bias, m, s, heat,
+                                        1.0, 4.0, True, 0.8))
+    want = torch.stack(outs)
+    assert torch.equal(planes, want), f"{int((planes != want).sum())} spikes differ"
+    if pool == "mean":
+        acc = want[0].clone()
+        for t in range(1, T - 1):
+            acc += want[t]
+        ref = (acc + want[T - 1]) * (1.0 / T) if T > 1 else want[0] * (1.0 / T)
+    else:
+        ref = want[T - 1]
+    assert torch.equal(pooled, ref)
+    assert 0.01 < float(want.mean()) < 0.99  # both spike values occur
