@@ -105,13 +105,14 @@ def _weight_image(W, K, N, sk, sn, wdt):
 
 
 # ----------------------------------------------------------------- spike -> CSR
-def csr_compact(S, values=True):
+def csr_compact(S, values=True, capacity=None):
     """Per-plane CSR of S [T, M, K] (or [M, K] as one plane).
 
     Returns a dict with nnz_row [T, M], row_ptr [T, M+1] (int32, relative to
     each plane), col_idx (int32, planes back to back), values (float32 or
-    None) and plane_ptr [T+1] (int64).  One launch for all planes (plus a
-    small device->host read of the total to size the outputs)."""
+    None) and plane_ptr [T+1] (int64).  One launch for all planes, into
+    buffers of `capacity` entries (default T*M*K, enough for any input), then
+    an 8-byte device->host read of the total to size the returned views."""
     require_cuda(S, what="csr_compact")
     require_f32(S, what="csr_compact")
     S = _contig(S)
@@ -123,14 +124,17 @@ def csr_compact(S, values=True):
     nnz_row = torch.empty(T, M, dtype=torch.int32, device=dev)
     row_ptr = torch.empty(T, M + 1, dtype=torch.int32, device=dev)
     plane_ptr = torch.empty(T + 1, dtype=torch.int64, device=dev)
-    cap = int((S > 0).sum().item())
+    cap = int(capacity) if capacity is not None else T * M * K
     col_idx = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
     vals = torch.empty(max(cap, 1), dtype=torch.float32, device=dev) if values else None
     ws, wsn = _lib.workspace(dev, lib.spk_csr_workspace_bytes(T, M, K))
     check(lib.spk_csr_compact(ptr(S), T, M, K, ptr(nnz_row), ptr(row_ptr), ptr(col_idx), ptr(vals),
                               ptr(plane_ptr), cap, ws, wsn, stream_of(S)), "spk_csr_compact")
-    return {"nnz_row": nnz_row, "row_ptr": row_ptr, "col_idx": col_idx[:cap],
-            "values": None if vals is None else vals[:cap], "plane_ptr": plane_ptr}
+    nnz = int(plane_ptr[T].item())
+    if nnz > cap:
+        raise EngineError(f"csr_compact: {nnz} spikes exceed the capacity of {cap}")
+    return {"nnz_row": nnz_row, "row_ptr": row_ptr, "col_idx": col_idx[:nnz],
+            "values": None if vals is None else vals[:nnz], "plane_ptr": plane_ptr}
 
 
 # ------------------------------------------------------------------ spike-linear
