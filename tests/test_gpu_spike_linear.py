@@ -422,3 +422,20 @@ def test_prepared_weight_image_through_the_c_abi():
     torch.cuda.synchronize()
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
     assert O.rel_err(ys[1].cpu().numpy(), O.spike_linear(S.cpu().numpy(), WT.cpu().numpy())) < TOL
+
+
+def test_weight_cache_never_serves_a_freed_weights_image():
+    """A new weight tensor allocated at a freed weight's address (the caching
+    allocator reuses blocks) with version 0 and the same shape must not be
+    given the old tensor's image: the cache holds the tensor by weak reference
+    and drops the image when the tensor dies."""
+    S = _spikes(2, 600, 256, 0.2, seed=51)
+    outs, refs = [], []
+    for seed in (52, 53, 54):
+        W = _weight(192, 256, seed=seed)
+        outs.append(ops.spike_linear(S, weight=W, branch="dense"))
+        refs.append(O.spike_linear(S.cpu().numpy(), W.t().cpu().numpy()))
+        del W
+    for y, ref in zip(outs, refs):
+        assert O.rel_err(y.cpu().numpy(), ref) < TOL
+    assert not torch.equal(outs[0], outs[1])
