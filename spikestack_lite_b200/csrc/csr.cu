@@ -87,6 +87,7 @@ struct CsrArgs {
   const uint32_t* bitmap;  // bitmap source: [T*M][KWP] planar spike masks written by the dense kernel
   const int32_t* row_cnt;  // bitmap source: [T*M] spikes per row
   int KWP;                 // planar words per row (2 per 64-column chunk)
+  int vec4;                // S rows 16-byte aligned (K % 4 == 0, aligned base): phase A reads float4
   const int32_t* blk_sum;                // bitmap source: spikes per 128-row block of the T*M rows
   const unsigned long long* sup_sum;     // bitmap source: spikes per 16384-row super-block
   const int* gate;         // automatic branch choice: run only when *gate == gate_value (null: always)
@@ -146,6 +147,44 @@ __global__ void __launch_bounds__(256) csr_scan_kernel(CsrArgs a) {
 
   // ---- phase A: ballot rows into the shared bitmap
   bool nonunit = false;
+  if (a.vec4) {
+    // 16-byte loads: lane l holds columns 4l .. 4l+3 of a 128-column block, so
+    // ballot e has bit l = column 4l + e; lane i < 4 interleaves byte i of the
+    // four ballots into the block's column-order word i (bit b = column 32i + b)
+    const int sh = (lane & 3) * 8;
+    for (int r = warp; r < RT; r += 8) {
+      int c = 0;
+      if (r < rows) {
+        const float4* row = reinterpret_cast<const float4*>(Sp + (int64_t)r * a.K);
+        const int nb = (a.K + 127) / 128;
+        for (int b0 = 0; b0 < nb; b0 += 4) {
+          float4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int col = (b0 + u) * 128 + 4 * lane;
+            v[u] = (b0 + u < nb && col < a.K) ? __ldg(row + (b0 + u) * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 x = v[u];
+            nonunit |= (x.x > 0.0f && x.x != 1.0f) || (x.y > 0.0f && x.y != 1.0f) || (x.z > 0.0f && x.z != 1.0f) ||
+                       (x.w > 0.0f && x.w != 1.0f);
+            const uint32_t m0 = __ballot_sync(0xffffffffu, x.x > 0.0f);
+            const uint32_t m1 = __ballot_sync(0xffffffffu, x.y > 0.0f);
+            const uint32_t m2 = __ballot_sync(0xffffffffu, x.z > 0.0f);
+            const uint32_t m3 = __ballot_sync(0xffffffffu, x.w > 0.0f);
+            c += __popc(m0) + __popc(m1) + __popc(m2) + __popc(m3);
+            const uint32_t word = spread8_stride4((m0 >> sh) & 0xffu) | (spread8_stride4((m1 >> sh) & 0xffu) << 1) |
+                                  (spread8_stride4((m2 >> sh) & 0xffu) << 2) |
+                                  (spread8_stride4((m3 >> sh) & 0xffu) << 3);
+            const int w = (b0 + u) * 4 + (lane & 3);
+            if (lane < 4 && b0 + u < nb && w < a.KW) bm[r * a.KW + w] = word;
+          }
+        }
+      }
+      if (lane == 0) cnt[r] = c;
+    }
+  } else
   for (int r = warp; r < RT; r += 8) {
     int c = 0;
     if (r < rows) {
@@ -575,6 +614,7 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
   a.KWP = 2 * (int)ceil_div(K, 64);
   a.blk_sum = blk_sum;
   a.sup_sum = sup_sum;
+  a.vec4 = (S != nullptr && K % 4 == 0 && (reinterpret_cast<uintptr_t>(S) & 15) == 0) ? 1 : 0;
   a.gate = gate.gate;
   a.gate_value = gate.gate_value;
   a.decide = gate.decide;

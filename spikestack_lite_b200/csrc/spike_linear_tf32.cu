@@ -102,7 +102,7 @@ __host__ __device__ __forceinline__ uint32_t sw128_chunk(uint32_t r, uint32_t c)
 // spike-linear predicate relu'(x) (x if x > 0, else 0) is applied to S; the
 // linear-activation op passes its input through unchanged (hi = x rounded
 // to tf32, lo = the remainder).
-template <int NS, int G, bool kRelu = true>
+template <int NS, int G, bool kRelu = true, bool kRev = false>
 __device__ __forceinline__ void tf32_converter(const int cw, const int lane, unsigned char* stg, uint64_t* stg_full,
                                                uint64_t* chk, uint64_t* stg_empty, uint64_t* lo_go,
                                                uint64_t* lo_full, uint8_t* lo_flag, int* row_count,
@@ -134,11 +134,12 @@ __device__ __forceinline__ void tf32_converter(const int cw, const int lane, uns
   uint32_t ps = 0u;  // phase parity of the current use of slot s
   bool ok = true;
   for (int g = 0; g < groups && ok; ++g) {
-    const int tg = min(G, tiles - g * G);
+    const int pg = kRev ? groups - 1 - g : g;  // the caller's group order
+    const int tg = min(G, tiles - pg * G);
     for (int kc = 0; kc < nk && ok; ++kc) {
       for (int t = 0; t < tg; ++t) {
         if (!(ok = mbar_wait(&stg_full[s], ps, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        const int64_t row0 = r_begin + (int64_t)(g * G + t) * t32::kRows;
+        const int64_t row0 = r_begin + (int64_t)(pg * G + t) * t32::kRows;
         const int nrows = (int)min64(t32::kRows, r_end - row0);
         unsigned char* st = stg + s * t32::kStgBytes;
         uint4 v[NL];  // raw fp32 bits; rows past nrows count as zero

@@ -130,12 +130,13 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
   int j = 0;
   bool ok = true;
   for (int g = 0; g < groups && ok; ++g) {
-    const int tg = min(G, tiles - g * G);
+    const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
     for (int kc = 0; kc < nk && ok; ++kc) {
       for (int t = 0; t < tg; ++t, ++j) {
         const int s = j % NS, l = j % NL;
         if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(g * G + t) * wt::kRows));
+        const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(pg * G + t) * wt::kRows));
         const unsigned char* st = stg + s * wt::kStgBytes;
         float4 lo[NLD];
 #pragma unroll
@@ -178,12 +179,13 @@ __device__ __forceinline__ void bits_converter(const int cw, const int lane, uns
   int j = 0;
   bool ok = true;
   for (int g = 0; g < groups && ok; ++g) {
-    const int tg = min(G, tiles - g * G);
+    const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
     for (int kc = 0; kc < nk && ok; ++kc) {
       for (int t = 0; t < tg; ++t, ++j) {
         const int s = j % NS;
         if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        const int64_t row = r_begin + (int64_t)(g * G + t) * wt::kRows + rl;
+        const int64_t row = r_begin + (int64_t)(pg * G + t) * wt::kRows + rl;
         const uint32_t w = row < r_end ? bits[row * KW + 2 * kc + (q >> 1)] : 0u;
         const uint32_t h = (w >> ((q & 1) * 16)) & 0xffffu;
         unsigned char* st = stg + s * wt::kStgBytes;
@@ -312,22 +314,24 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       };
       int pre = 0;  // slots requested before the wait: the first NS (or all), only when S is known complete
       for (int g = 0; g < groups && pre < NS && a.early_s; ++g) {
-        const int tg = min(G, tiles - g * G);
+        const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
         for (int kc = 0; kc < nk && pre < NS; ++kc)
-          for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(g * G + t) * wt::kRows, kc);
+          for (int t = 0; t < tg && pre < NS; ++t, ++pre) load_s(pre, r_begin + (int64_t)(pg * G + t) * wt::kRows, kc);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
       int j = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
-        const int tg = min(G, tiles - g * G);
+        const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
         for (int kc = 0; kc < nk && ok; ++kc) {
           for (int t = 0; t < tg; ++t, ++j) {
             if (j < pre) continue;
             const int s = j % NS;
             if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
               break;
-            load_s(s, r_begin + (int64_t)(g * G + t) * wt::kRows, kc);
+            load_s(s, r_begin + (int64_t)(pg * G + t) * wt::kRows, kc);
           }
         }
       }
@@ -343,7 +347,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       int j = 0, ja = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
-        const int tg = min(G, tiles - g * G);
+        const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
         // the accumulators are single-buffered: the previous group's epilogue has read them
         if (g >= 1 && !(ok = mbar_wait(acc_empty, (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         tc_fence_after();
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, lo_flag, abort_flag, a.bits_in, a.K / 32, r_begin,
                             r_end, nk, groups, tiles);
     } else {
-      tf32_converter<NS, G, kRelu>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count,
+      tf32_converter<NS, G, kRelu, true>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count,
                                    abort_flag, a, r_begin, r_end, n_tile, nk, groups, tiles);
     }
   } else {
@@ -492,7 +497,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       return true;
     };
     for (int g = 0; g < groups && ok; ++g) {
-      const int tg = min(G, tiles - g * G);
+      const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
+    const int tg = min(G, tiles - pg * G);
       // this group's chunks, then the next group's first two (their buffers
       // free up with this group's last MMAs), then this group's epilogue
       while (ok && ja < min(total_chunks, (g + 1) * nk + 2)) ok = load_chunk();
@@ -500,7 +506,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       if (!(ok = mbar_wait(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
       tc_fence_after();
       for (int t = 0; t < tg; ++t) {
-        const int64_t row0 = r_begin + (int64_t)(g * G + t) * wt::kRows;
+        const int64_t row0 = r_begin + (int64_t)(pg * G + t) * wt::kRows;
 #pragma unroll 1
         for (int rb = 0; rb < wt::kRows; rb += 16) {
           if (row0 + rb >= r_end) break;
