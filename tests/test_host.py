@@ -157,3 +157,31 @@ def test_engine_objects_expose_reference_names():
         assert callable(getattr(E.attention_engine, name))
     assert callable(E.gsmc_engine.fused_gsmc_step)
     assert callable(E.spire_engine.spire_dither)
+
+
+def test_install_into_the_reference_package_when_available():
+    """With a checkout of the reference named by SPIKESTACK_REFERENCE, install
+    the engine into the real `spikestack_lite` package: its sparse, attention,
+    GSMC and Spire modules then hold this engine's objects, and the reference's
+    own SparseLinear reports the engine present.  Skipped without a checkout."""
+    import importlib
+    import os
+    import sys
+
+    ref = os.environ.get("SPIKESTACK_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "spikestack_lite")):
+        pytest.skip("no reference checkout (set SPIKESTACK_REFERENCE)")
+    sys.path.insert(0, ref)
+    try:
+        pkg = importlib.import_module("spikestack_lite")
+        E.install(pkg)
+        sparse = importlib.import_module("spikestack_lite.sparse")
+        attn = importlib.import_module("spikestack_lite.nn.attention")
+        gsmc = importlib.import_module("spikestack_lite.nn.gsmc")
+        assert sparse._cuda_engine is E.sparse_engine
+        assert attn._attn_cuda_engine is E.attention_engine
+        assert gsmc._gsmc_cuda_engine is E.gsmc_engine
+    finally:
+        sys.path.remove(ref)
+        for n in [m for m in sys.modules if m == "spikestack_lite" or m.startswith("spikestack_lite.")]:
+            sys.modules.pop(n, None)
