@@ -75,7 +75,8 @@ def test_fused_recurrence_vs_oracle_engine_order():
     assert frac < 1e-3
 
 
-@pytest.mark.parametrize("M,d,T,pool", [(4096, 512, 4, "mean"), (1000, 64, 3, "last"), (333, 96, 2, "mean")])
+@pytest.mark.parametrize("M,d,T,pool", [(4096, 512, 4, "mean"), (1000, 64, 3, "last"), (333, 96, 2, "mean"),
+                                         (1, 32, 2, "mean"), (130, 32, 5, "last")])
 def test_fused_recurrence_matches_the_two_kernel_form(M, d, T, pool):
     """The fused recurrence (gate projections W_rec s_{t-1} in tensor memory,
     cell update in the same kernel's epilogue) gives exactly the spikes and the
@@ -109,4 +110,5 @@ def test_fused_recurrence_matches_the_two_kernel_form(M, d, T, pool):
     else:
         ref = want[T - 1]
     assert torch.equal(pooled, ref)
-    assert 0.01 < float(want.mean()) < 0.99  # both spike values occur
+    if M * d >= 1000:
+        assert 0.01 < float(want.mean()) < 0.99  # both spike values occur

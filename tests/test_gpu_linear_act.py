@@ -134,3 +134,13 @@ def test_spike_linear_bits_matches_the_unpacked_dense_branch(T, M, K, N):
     assert torch.equal(y_bits, y_dense)
     ref = S.cpu().double() @ w.cpu().double().t() + b.cpu().double()
     assert float((y_bits.cpu().double() - ref).abs().max() / ref.abs().max()) < 1e-4
+
+
+def test_packed_paths_with_no_rows():
+    """Empty inputs: the packed epilogue and the packed spike-linear return
+    empty outputs without launching."""
+    w = torch.randn(128, 64, device="cuda")
+    x = torch.empty(0, 64, device="cuda")
+    assert ops.linear_act(x, w, None, act="heaviside_bits").shape == (0, 4)
+    bits = torch.empty(3, 0, 2, dtype=torch.int32, device="cuda")
+    assert ops.spike_linear_bits(bits, 64, w).shape == (3, 0, 128)

@@ -439,3 +439,17 @@ def test_weight_cache_never_serves_a_freed_weights_image():
     for y, ref in zip(outs, refs):
         assert O.rel_err(y.cpu().numpy(), ref) < TOL
     assert not torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("T,M", [(1, 5), (2, 700)])
+def test_auto_branch_small_inputs(T, M):
+    """The automatic choice on inputs with fewer rows than the probe samples:
+    the result is one of the two branches' outputs exactly."""
+    K, N = 2048, 512
+    S = _spikes(T, M, K, 0.003, seed=M)
+    W = _weight(N, K, seed=3, dtype=torch.bfloat16)
+    got = ops.spike_linear(S, weight=W, branch="auto")
+    assert torch.equal(got, ops.spike_linear(S, weight=W, branch="csr")) or \
+        torch.equal(got, ops.spike_linear(S, weight=W, branch="dense"))
+    ref = O.spike_linear(S.cpu().numpy(), W.float().t().cpu().numpy())
+    assert O.rel_err(got.cpu().numpy(), ref) < TOL
