@@ -191,13 +191,15 @@ int spk_sparse_multistep_forward(const float* dense_input, int T, int64_t B, int
  * fp32-accurate on the tensor cores (tf32 hi/lo splits of W and X).  Needs
  * N > 64, K % 4 == 0 and a 16-byte aligned X.  Replaces the nn.Linear +
  * threshold + Heaviside pairs around the spike-linear path. */
-enum { SPK_ACT_NONE = 0, SPK_ACT_HEAVISIDE = 1, SPK_ACT_VSPIKE = 2, SPK_ACT_HEAVISIDE_BITS = 3 };
+enum { SPK_ACT_NONE = 0, SPK_ACT_HEAVISIDE = 1, SPK_ACT_VSPIKE = 2, SPK_ACT_HEAVISIDE_BITS = 3, SPK_ACT_VSPIKE_BITS = 4 };
 /* SPK_ACT_HEAVISIDE_BITS: the Heaviside spikes of SPK_ACT_HEAVISIDE packed one
  * bit each, Y read as uint32 [R][N/32] (bit b of word w of a row = column
  * 32w + b; N % 32 == 0): 32x fewer bytes than the fp32 spike tensor for the
  * layer that consumes them (spk_spike_linear_bits).  Replaces the dense fp32
  * act tensor of SpikingFFN (attention.py:156), which the reference writes
- * and fc2 reads back. */
+ * and fc2 reads back.  SPK_ACT_VSPIKE_BITS packs the SPK_ACT_VSPIKE spikes the
+ * same way (the attention's v, attention.py:114-115; q and k use
+ * SPK_ACT_HEAVISIDE_BITS with thr 0) for spk_spiking_attention_bits. */
 size_t spk_linear_act_workspace_bytes(int K, int N);
 int spk_linear_act(const float* X, int64_t R, int K, const float* W, int64_t w_stride_k, int64_t w_stride_n, int N,
                    const float* bias, int act, float thr, float* Y, void* workspace, size_t workspace_bytes,
@@ -237,6 +239,16 @@ size_t spk_attention_workspace_bytes(int64_t BT, int L, int H, int dh);
 int spk_spiking_attention(const float* q, const float* k, const float* v, const float* lam, int64_t BT, int L,
                           int H, int dh, float eps, float* out, void* workspace, size_t workspace_bytes,
                           spk_stream_t stream);
+/* The same over packed spikes: q_bits, k_bits, v_bits uint32 [BT*L][d/32]
+ * (bit b of word w = channel 32w + b, as SPK_ACT_HEAVISIDE_BITS /
+ * SPK_ACT_VSPIKE_BITS write them), 32x fewer input bytes; out as above,
+ * bit-identical to spk_spiking_attention on the unpacked spikes.  Needs
+ * d % 128 == 0 and dh in {16, 32, 64}; workspace as spk_attention_workspace_bytes.
+ * Replaces the three fp32 spike tensors between the reference's q/k/v
+ * projections and its attention (attention.py:110-117). */
+int spk_spiking_attention_bits(const uint32_t* q_bits, const uint32_t* k_bits, const uint32_t* v_bits,
+                               const float* lam, int64_t BT, int L, int H, int dh, float eps, float* out,
+                               void* workspace, size_t workspace_bytes, spk_stream_t stream);
 
 /* ------------------------------------------------------- GSMC
  * fused_gsmc_step (gsmc_cuda.cu:11-127): one cell step over M rows of width d;

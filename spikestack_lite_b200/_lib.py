@@ -52,6 +52,7 @@ SIGNATURES = {
     "spk_normalize_attention": (_I, [_P, _P, _L, _F, _P, _P]),
     "spk_attention_workspace_bytes": (_Z, [_L, _I, _I, _I]),
     "spk_spiking_attention": (_I, [_P, _P, _P, _P, _L, _I, _I, _I, _F, _P, _P, _Z, _P]),
+    "spk_spiking_attention_bits": (_I, [_P, _P, _P, _P, _L, _I, _I, _I, _F, _P, _P, _Z, _P]),
     "spk_gsmc_step": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _L, _I, _F, _F, _I, _F, _P]),
     "spk_gsmc_workspace_bytes": (_Z, [_L, _I]),
     "spk_gsmc_forward": (_I, [_P, _P, _P, _P, _I, _L, _I, _F, _F, _I, _F, _I, _P, _P, _P, _Z, _P]),

@@ -139,11 +139,34 @@ class AstrocyteHebbianAttention(nn.Module):
                                                 _attn_cuda_engine)
         return out.transpose(-3, -2).contiguous().view(*leading, d)
 
+    def _packed_ok(self, x):
+        """Inference on shapes the packed tensor-core attention takes."""
+        d = self.h * self.dh
+        return (not torch.is_grad_enabled() and x.is_cuda and x.dtype == torch.float32 and self.L == 1
+                and d % 128 == 0 and self.dh in (16, 32, 64))
+
     def forward(self, x, record=None):
         """``record`` (a dict, optional) receives the q, k, v spikes and the
-        normalised attention ("attn") this call computed."""
+        normalised attention ("attn") this call computed.
+
+        At inference the q, k and v spikes go from their projections to the
+        attention packed one bit each (linear_act "heaviside_bits" /
+        "vspike_bits" -> spiking_attention_bits): the reference's three fp32
+        spike tensors (attention.py:110-117) are never written."""
         if x.device.type != "cuda":
             raise EngineError("AstrocyteHebbianAttention: CUDA input required (no CPU path)")
+        if self._packed_ok(x):
+            qb = engine_linear(self.q_proj, x, "heaviside_bits")
+            if qb is not None:
+                kb = engine_linear(self.k_proj, x, "heaviside_bits")
+                vb = engine_linear(self.v_proj, x, "vspike_bits", 0.5)  # tau[0] = 1 / (L + 1), L = 1
+                a = ops.spiking_attention_bits(qb, kb, vb, torch.sigmoid(self.decay_logit), self.h, self.eps)
+                if record is not None:
+                    d = self.h * self.dh
+                    record.update(q=ops.unpack_spikes(qb, d), k=ops.unpack_spikes(kb, d), v=ops.unpack_spikes(vb, d),
+                                  attn=a)
+                y = engine_linear(self.o_proj, a)
+                return y if y is not None else self.o_proj(a)
         q, k, v = self.spikes(x)
         a = self.attend(q, k, v)
         if record is not None:

@@ -38,6 +38,10 @@ namespace at {
 constexpr int kGrp = 128;                        // channels per head group
 constexpr int kBoxCols = 64, kBoxRows = 32;      // TMA box: 64 fp32 columns x 32 rows
 constexpr int kBoxBytes = kBoxCols * kBoxRows * 4;
+// packed spikes (32 channels per word): a head group's 128 channels are 4 words = 16 bytes per position
+constexpr int kBitWords = kGrp / 32;
+constexpr int kBitBox1 = kBitWords * 32 * 4;     // pass 1: 32 positions
+constexpr int kBitBox2 = kBitWords * 128 * 4;    // pass 2: one 128-position tile
 constexpr int kConvWarps = 8;
 constexpr int kThreads = 32 * (2 + kConvWarps + 4);
 
@@ -99,7 +103,9 @@ __device__ __forceinline__ uint32_t p1_offset(int p, int c) {
 
 __device__ __forceinline__ uint32_t upper_halves(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x7632); }
 
-template <int DH>
+// kBits: k and v arrive packed (uint32 words [BT*L][d/32]); the converters
+// expand them to the same fp32 0 / 1 patterns the fp32 staging would hold.
+template <int DH, bool kBits = false>
 __global__ void __launch_bounds__(at::kThreads, 1)
     attn_kv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_tab, AttnKvArgs a) {
@@ -176,13 +182,19 @@ __global__ void __launch_bounds__(at::kThreads, 1)
           const int s = j % kNS1;
           if (j >= kNS1 && !(ok = mbar_wait(&stg_empty[s], ((j / kNS1) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
             break;
-          mbar_arrive_expect_tx(&stg_full[s], kStg1);
           unsigned char* st = stg + s * kStg1;
           const int row = (int)(bt * a.L) + c * kP1;
-          tma_load_2d(st + 0 * kBoxBytes, &tm_k, col, row, &stg_full[s]);
-          tma_load_2d(st + 1 * kBoxBytes, &tm_k, col + 64, row, &stg_full[s]);
-          tma_load_2d(st + 2 * kBoxBytes, &tm_v, col, row, &stg_full[s]);
-          tma_load_2d(st + 3 * kBoxBytes, &tm_v, col + 64, row, &stg_full[s]);
+          if constexpr (kBits) {  // one 16-byte-wide box of words each for k and v
+            mbar_arrive_expect_tx(&stg_full[s], 2 * kBitBox1 + 2 * kBoxBytes);
+            tma_load_2d(st + 0 * kBoxBytes, &tm_k, col / 32, row, &stg_full[s]);
+            tma_load_2d(st + 2 * kBoxBytes, &tm_v, col / 32, row, &stg_full[s]);
+          } else {
+            mbar_arrive_expect_tx(&stg_full[s], kStg1);
+            tma_load_2d(st + 0 * kBoxBytes, &tm_k, col, row, &stg_full[s]);
+            tma_load_2d(st + 1 * kBoxBytes, &tm_k, col + 64, row, &stg_full[s]);
+            tma_load_2d(st + 2 * kBoxBytes, &tm_v, col, row, &stg_full[s]);
+            tma_load_2d(st + 3 * kBoxBytes, &tm_v, col + 64, row, &stg_full[s]);
+          }
           tma_load_2d(st + 4 * kBoxBytes, &tm_tab, col, c * kP1, &stg_full[s]);
           tma_load_2d(st + 5 * kBoxBytes, &tm_tab, col + 64, c * kP1, &stg_full[s]);
           ++j;
@@ -255,8 +267,14 @@ __global__ void __launch_bounds__(at::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int off = box * kBoxBytes + (4 * cw + i) * 256 + cc * 4;
-          kk[i] = *reinterpret_cast<const uint4*>(st + off);
-          vv[i] = *reinterpret_cast<const uint4*>(st + 2 * kBoxBytes + off);
+          if constexpr (kBits) {
+            const int wi = (4 * cw + i) * kBitWords + (ch >> 5);
+            kk[i] = nibble_f32x4(reinterpret_cast<const uint32_t*>(st)[wi] >> (ch & 31));
+            vv[i] = nibble_f32x4(reinterpret_cast<const uint32_t*>(st + 2 * kBoxBytes)[wi] >> (ch & 31));
+          } else {
+            kk[i] = *reinterpret_cast<const uint4*>(st + off);
+            vv[i] = *reinterpret_cast<const uint4*>(st + 2 * kBoxBytes + off);
+          }
           ww[i] = *reinterpret_cast<const float4*>(st + 4 * kBoxBytes + off);
         }
         const int nvalid = min(kP1, a.L - c * kP1);
@@ -425,7 +443,8 @@ __global__ void __launch_bounds__(at::kThreads, 1)
   }
 }
 
-template <int DH>
+// kBits: q arrives packed (uint32 words [BT*L][d/32]), expanded by the converters.
+template <int DH, bool kBits = false>
 __global__ void __launch_bounds__(at::kThreads, 1)
     attn_out_tc_kernel(const __grid_constant__ CUtensorMap tm_q, AttnOutArgs a) {
   using namespace at;
@@ -500,10 +519,15 @@ __global__ void __launch_bounds__(at::kThreads, 1)
           const int s = js % kNS2;
           if (js >= kNS2 && !(ok = mbar_wait(&stg_empty[s], ((js / kNS2) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
             break;
-          mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(nbox * kBoxBytes));
-          for (int b = 0; b < nbox; ++b)
-            tma_load_2d(stg + s * kStg2 + b * kBoxBytes, &tm_q, col + 64 * kc,
-                        (int)(bt * a.L) + tile * kRows2 + kBoxRows * b, &stg_full[s]);
+          if constexpr (kBits) {  // the tile's 128 positions x 4 words (both K chunks read their half)
+            mbar_arrive_expect_tx(&stg_full[s], (uint32_t)kBitBox2);
+            tma_load_2d(stg + s * kStg2, &tm_q, col / 32, (int)(bt * a.L) + tile * kRows2, &stg_full[s]);
+          } else {
+            mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(nbox * kBoxBytes));
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(stg + s * kStg2 + b * kBoxBytes, &tm_q, col + 64 * kc,
+                          (int)(bt * a.L) + tile * kRows2 + kBoxRows * b, &stg_full[s]);
+          }
           ++js;
           if (kc == 0 && u != cur) {
             // a new unit: its kv image replaces the old one once every MMA on it is done
@@ -592,8 +616,15 @@ __global__ void __launch_bounds__(at::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int rl = 16 * cw + 2 * i + (lane >> 4);
-          v[i] = (rl < nrows) ? *reinterpret_cast<const uint4*>(stg + s * kStg2 + rl * 256 + kq * 4)
-                              : make_uint4(0u, 0u, 0u, 0u);
+          if constexpr (kBits) {
+            const int c = 64 * kc + kq;  // channel within the group
+            v[i] = (rl < nrows) ? nibble_f32x4(reinterpret_cast<const uint32_t*>(stg + s * kStg2)[rl * kBitWords + (c >> 5)] >>
+                                               (c & 31))
+                                : make_uint4(0u, 0u, 0u, 0u);
+          } else {
+            v[i] = (rl < nrows) ? *reinterpret_cast<const uint4*>(stg + s * kStg2 + rl * 256 + kq * 4)
+                                : make_uint4(0u, 0u, 0u, 0u);
+          }
         }
         unsigned char* ahi = a_hi + sa * kA2;
         uint32_t low = 0u;
@@ -716,11 +747,11 @@ inline size_t attn_tc_image_bytes(int64_t BT, int H, int dh) {
   return (size_t)BT * (size_t)((int64_t)H * dh / at::kGrp) * at::kImgBytes;
 }
 
-template <int DH>
+template <int DH, bool kBits = false>
 int launch_attention_tc_inst(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const CUtensorMap& mt, AttnKvArgs ka, AttnOutArgs oa, cudaStream_t st) {
-  auto k1 = attn_kv_tc_kernel<DH>;
-  auto k2 = attn_out_tc_kernel<DH>;
+  auto k1 = attn_kv_tc_kernel<DH, kBits>;
+  auto k2 = attn_out_tc_kernel<DH, kBits>;
   SPK_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at::kSmem1));
   SPK_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at::kSmem2));
   const int sms = sm_count();
@@ -737,16 +768,25 @@ int launch_attention_tc_inst(const CUtensorMap& mq, const CUtensorMap& mk, const
   return SPK_OK;
 }
 
-// tab: [L, d] decay table (written here), img: per-unit kv images.
-inline int launch_attention_tc(const float* q, const float* k, const float* v, const float* lam, int64_t BT, int L,
+// tab: [L, d] decay table (written here), img: per-unit kv images.  bits:
+// q, k, v are packed uint32 words [BT*L][d/32] instead of fp32.
+inline int launch_attention_tc(const void* q, const void* k, const void* v, const float* lam, int64_t BT, int L,
                                int H, int dh, float eps, float* out, float* tab, unsigned char* img,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool bits = false) {
   const int d = H * dh;
   const int64_t R = BT * (int64_t)L;
   CUtensorMap mq, mk, mv, mt;
-  int rc = make_map_2d_f32(&mq, q, R, d, d, at::kBoxCols, at::kBoxRows, "q");
-  if (!rc) rc = make_map_2d_f32(&mk, k, R, d, d, at::kBoxCols, at::kBoxRows, "k");
-  if (!rc) rc = make_map_2d_f32(&mv, v, R, d, d, at::kBoxCols, at::kBoxRows, "v");
+  int rc;
+  if (bits) {
+    const int W = d / 32;
+    rc = make_map_2d_u32(&mq, static_cast<const uint32_t*>(q), R, W, W, at::kBitWords, at::kRows2, "q bits");
+    if (!rc) rc = make_map_2d_u32(&mk, static_cast<const uint32_t*>(k), R, W, W, at::kBitWords, at::kP1, "k bits");
+    if (!rc) rc = make_map_2d_u32(&mv, static_cast<const uint32_t*>(v), R, W, W, at::kBitWords, at::kP1, "v bits");
+  } else {
+    rc = make_map_2d_f32(&mq, static_cast<const float*>(q), R, d, d, at::kBoxCols, at::kBoxRows, "q");
+    if (!rc) rc = make_map_2d_f32(&mk, static_cast<const float*>(k), R, d, d, at::kBoxCols, at::kBoxRows, "k");
+    if (!rc) rc = make_map_2d_f32(&mv, static_cast<const float*>(v), R, d, d, at::kBoxCols, at::kBoxRows, "v");
+  }
   if (!rc) rc = make_map_2d_f32(&mt, tab, L, d, d, at::kBoxCols, at::kBoxRows, "decay table");
   if (rc) return rc;
   decay_table_kernel<<<grid_for((int64_t)L * d, 256), 256, 0, st>>>(lam, L, d, tab);
@@ -766,10 +806,18 @@ inline int launch_attention_tc(const float* q, const float* k, const float* v, c
   oa.eps = eps;
   oa.img = img;
   oa.out = out;
-  switch (dh) {
-    case 16: rc = launch_attention_tc_inst<16>(mq, mk, mv, mt, ka, oa, st); break;
-    case 32: rc = launch_attention_tc_inst<32>(mq, mk, mv, mt, ka, oa, st); break;
-    default: rc = launch_attention_tc_inst<64>(mq, mk, mv, mt, ka, oa, st); break;
+  if (bits) {
+    switch (dh) {
+      case 16: rc = launch_attention_tc_inst<16, true>(mq, mk, mv, mt, ka, oa, st); break;
+      case 32: rc = launch_attention_tc_inst<32, true>(mq, mk, mv, mt, ka, oa, st); break;
+      default: rc = launch_attention_tc_inst<64, true>(mq, mk, mv, mt, ka, oa, st); break;
+    }
+  } else {
+    switch (dh) {
+      case 16: rc = launch_attention_tc_inst<16>(mq, mk, mv, mt, ka, oa, st); break;
+      case 32: rc = launch_attention_tc_inst<32>(mq, mk, mv, mt, ka, oa, st); break;
+      default: rc = launch_attention_tc_inst<64>(mq, mk, mv, mt, ka, oa, st); break;
+    }
   }
   if (rc) return rc;
   count_launch(3);
@@ -827,4 +875,28 @@ extern "C" int spk_spiking_attention(const float* q, const float* k, const float
   SPK_LAUNCH_CHECK();
   spk::count_launch(3);
   return SPK_OK;
+}
+
+// The same attention over packed q, k, v spikes (uint32 words [BT*L][d/32],
+// bit b of word w = channel 32w + b), as the model's projections write them:
+// 32x fewer input bytes, results bit-identical to spk_spiking_attention on the
+// unpacked spikes.  Tensor-core path only: d % 128 == 0, dh in {16, 32, 64}.
+extern "C" int spk_spiking_attention_bits(const uint32_t* q_bits, const uint32_t* k_bits, const uint32_t* v_bits,
+                                          const float* lam, int64_t BT, int L, int H, int dh, float eps, float* out,
+                                          void* workspace, size_t workspace_bytes, spk_stream_t stream) {
+  SPK_REQUIRE(q_bits && k_bits && v_bits && lam && out, "q_bits, k_bits, v_bits, lam and out must be non-null");
+  SPK_REQUIRE(BT >= 1 && L >= 1 && H >= 1, "invalid shape");
+  SPK_REQUIRE(dh == 16 || dh == 32 || dh == 64, "head width %d not supported (16, 32 or 64)", dh);
+  SPK_REQUIRE(((int64_t)H * dh) % spk::at::kGrp == 0, "packed attention needs d %% 128 == 0 (d=%d)", H * dh);
+  SPK_REQUIRE(BT * (int64_t)L < (1ll << 31), "BT*L must stay below 2^31 rows");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q_bits) | reinterpret_cast<uintptr_t>(k_bits) |
+                       reinterpret_cast<uintptr_t>(v_bits) | reinterpret_cast<uintptr_t>(out);
+  SPK_REQUIRE((al & 15) == 0, "q_bits, k_bits, v_bits and out must be 16-byte aligned");
+  const spk::AttnLayout A = spk::attn_layout(BT, L, H, dh);
+  if (workspace == nullptr || workspace_bytes < A.total)
+    return spk::fail(SPK_EWORKSPACE, "workspace of %zu bytes required", A.total);
+  float* tab = reinterpret_cast<float*>(static_cast<char*>(workspace) + A.tab);
+  unsigned char* img = reinterpret_cast<unsigned char*>(static_cast<char*>(workspace) + A.kv);
+  return spk::launch_attention_tc(q_bits, k_bits, v_bits, lam, BT, L, H, dh, eps, out, tab, img,
+                                  (cudaStream_t)stream, true);
 }

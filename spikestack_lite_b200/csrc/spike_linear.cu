@@ -400,8 +400,9 @@ static int linear_act_impl(const float* X, int64_t R, int K, const float* W, int
   SPK_REQUIRE(R >= 0 && K >= 1 && N >= 1, "bad shape R=%lld K=%d N=%d", (long long)R, K, N);
   SPK_REQUIRE(R < (int64_t(1) << 31), "linear_act: at most 2^31 - 1 rows per call (TMA row coordinates)");
   SPK_REQUIRE(W && (R == 0 || (X && Y)), "X, W and Y must be non-null");
-  SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_HEAVISIDE_BITS, "unknown activation %d", act);
-  SPK_REQUIRE(act != SPK_ACT_HEAVISIDE_BITS || N % 32 == 0, "packed spikes need N %% 32 == 0 (N=%d)", N);
+  SPK_REQUIRE(act >= SPK_ACT_NONE && act <= SPK_ACT_VSPIKE_BITS, "unknown activation %d", act);
+  SPK_REQUIRE((act != SPK_ACT_HEAVISIDE_BITS && act != SPK_ACT_VSPIKE_BITS) || N % 32 == 0,
+              "packed spikes need N %% 32 == 0 (N=%d)", N);
   SPK_REQUIRE(N > 64, "linear_act needs N > 64 (128-column tiles on the tensor cores)");
   SPK_REQUIRE(K % 4 == 0 && (R == 0 || tc_supported(K, N, X)), "linear_act needs K %% 4 == 0 and a 16-byte aligned X");
   const TcPlan p = tc_plan(K, N, SPK_F32);

@@ -91,7 +91,8 @@ enum WtEpilogue : int {
   kEpiHeaviside = 1,  // 1 if y - thr > 0 else 0 (spike_fn(fc1(x) - thr); q, k spikes with thr = 0)
   kEpiVSpike = 2,     // 1 if (tanh(y) + 1) / 2 - thr > 0 else 0 (the v spikes, thr = tau)
   kEpiHeavisideBits = 3,  // the Heaviside spikes packed: bit b of word w of a row = column 32w + b
-  kEpiGsmc = 4            // the GSMC cell update from the recurrent gate projections (a.cell)
+  kEpiVSpikeBits = 4,     // the v spikes packed the same way
+  kEpiGsmc = 5            // the GSMC cell update from the recurrent gate projections (a.cell)
 };
 
 template <int kEpi>
@@ -539,14 +540,16 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
                 gsmc_update(a.cell, row, ch, cin[r4], xb[(0 * 16 + rr) * 32 + lane], xb[(1 * 16 + rr) * 32 + lane],
                             xb[(2 * 16 + rr) * 32 + lane], xb[(3 * 16 + rr) * 32 + lane]);
             }
-          } else if constexpr (kEpi == kEpiHeavisideBits) {
+          } else if constexpr (kEpi == kEpiHeavisideBits || kEpi == kEpiVSpikeBits) {
             // one ballot per row gives the row's word of this warp's 32 columns (N % 32 == 0:
             // a warp's columns are all in range or all out); lane jj stores row rb + jj's word
             if (n0 + q * 32 < a.N) {
               uint32_t word = 0u;
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj) {
-                const uint32_t b = __ballot_sync(0xffffffffu, v[jj] + bias_n - a.thr > 0.0f);
+                const float spike = wt_epilogue<kEpi == kEpiHeavisideBits ? kEpiHeaviside : kEpiVSpike>(
+                    v[jj] + bias_n, a.thr);
+                const uint32_t b = __ballot_sync(0xffffffffu, spike > 0.0f);
                 if (lane == jj) word = b;
               }
               const int NW = a.N / 32;
@@ -625,7 +628,8 @@ inline TcArgs wt_args(int64_t R, int K, int N, const TcPlan& p, const unsigned c
 int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o,
               cudaStream_t stream, int act = -1, float thr = 0.0f) {
   if (p.NT != wt::kLanes) return fail(SPK_EINVAL, "weights-in-TMEM kernel needs 128-column N tiles (NT=%d)", p.NT);
-  if (act == kEpiHeavisideBits && N % 32 != 0) return fail(SPK_EINVAL, "packed spikes need N %% 32 == 0 (N=%d)", N);
+  if ((act == kEpiHeavisideBits || act == kEpiVSpikeBits) && N % 32 != 0)
+    return fail(SPK_EINVAL, "packed spikes need N %% 32 == 0 (N=%d)", N);
   CUtensorMap map;
   int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
   if (rc) return rc;
@@ -636,6 +640,7 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
     case kEpiHeaviside: return launch_wt_inst<kEpiHeaviside, false>(map, a, p.n_tiles, stream);
     case kEpiVSpike: return launch_wt_inst<kEpiVSpike, false>(map, a, p.n_tiles, stream);
     case kEpiHeavisideBits: return launch_wt_inst<kEpiHeavisideBits, false>(map, a, p.n_tiles, stream);
+    case kEpiVSpikeBits: return launch_wt_inst<kEpiVSpikeBits, false>(map, a, p.n_tiles, stream);
     default: break;
   }
   return fail(SPK_EINVAL, "unknown activation %d", act);

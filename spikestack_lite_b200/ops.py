@@ -187,7 +187,7 @@ def spike_linear(S, weight=None, weightT=None, bias=None, branch="auto", csr=Non
     return Y[0] if squeeze else Y
 
 
-_ACTS = {"none": 0, "heaviside": 1, "vspike": 2, "heaviside_bits": 3}
+_ACTS = {"none": 0, "heaviside": 1, "vspike": 2, "heaviside_bits": 3, "vspike_bits": 4}
 
 
 def linear_act(x, weight, bias=None, act="none", thr=0.0):
@@ -199,6 +199,7 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
       "vspike"     ((tanh(y) + 1) / 2 - thr > 0).float()  v spikes (thr = tau)
       "heaviside_bits"  the "heaviside" spikes packed 32 to an int32 word:
                    [..., N/32], bit b of word w = column 32w + b (N % 32 == 0)
+      "vspike_bits"     the "vspike" spikes packed the same way
 
     Needs N > 64 and K % 4 == 0."""
     require_cuda(x, weight, bias, what="linear_act")
@@ -215,7 +216,7 @@ def linear_act(x, weight, bias=None, act="none", thr=0.0):
         if bias.numel() != N:
             raise EngineError("linear_act: bias must have N elements")
     R = x.numel() // K if K else 0
-    if act == "heaviside_bits":
+    if act in ("heaviside_bits", "vspike_bits"):
         if N % 32:
             raise EngineError(f"linear_act: packed spikes need N % 32 == 0 (N={N})")
         Y = torch.empty(*x.shape[:-1], N // 32, dtype=torch.int32, device=x.device)
@@ -410,6 +411,34 @@ def spiking_attention(q, k, v, lam, heads, eps=1e-6):
     ws, wsn = _lib.workspace(q.device, lib.spk_attention_workspace_bytes(BT, L, heads, dh))
     check(lib.spk_spiking_attention(ptr(q), ptr(k), ptr(v), ptr(lam), BT, L, heads, dh, float(eps), ptr(out), ws,
                                     wsn, stream_of(q)), "spk_spiking_attention")
+    return out
+
+
+def spiking_attention_bits(q_bits, k_bits, v_bits, lam, heads, eps=1e-6):
+    """spiking_attention over packed spikes: q_bits, k_bits, v_bits int32
+    [..., L, d/32] (bit b of word w = channel 32w + b, as linear_act's
+    "heaviside_bits" / "vspike_bits" write them) -> [..., L, d] fp32, the same
+    values as spiking_attention on the unpacked spikes.  Needs d % 128 == 0."""
+    require_cuda(q_bits, k_bits, v_bits, lam, what="spiking_attention_bits")
+    require_f32(lam, what="spiking_attention_bits")
+    shape = q_bits.shape
+    if k_bits.shape != shape or v_bits.shape != shape:
+        raise EngineError("spiking_attention_bits: q, k and v must have the same shape")
+    for t in (q_bits, k_bits, v_bits):
+        if t.dtype != torch.int32:
+            raise EngineError("spiking_attention_bits: packed spikes must be int32")
+    L, d = shape[-2], shape[-1] * 32
+    if d % heads:
+        raise EngineError("spiking_attention_bits: d_model must be divisible by heads")
+    dh = d // heads
+    q_bits, k_bits, v_bits, lam = (_contig(t) for t in (q_bits, k_bits, v_bits, lam))
+    BT = q_bits.numel() // (L * (d // 32))
+    out = torch.empty(*shape[:-1], d, dtype=torch.float32, device=q_bits.device)
+    lib = _lib.load()
+    ws, wsn = _lib.workspace(q_bits.device, lib.spk_attention_workspace_bytes(BT, L, heads, dh))
+    check(lib.spk_spiking_attention_bits(ptr(q_bits), ptr(k_bits), ptr(v_bits), ptr(lam), BT, L, heads, dh,
+                                         float(eps), ptr(out), ws, wsn, stream_of(q_bits)),
+          "spk_spiking_attention_bits")
     return out
 
 

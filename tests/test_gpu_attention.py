@@ -111,3 +111,27 @@ def test_tensor_core_attention_zero_keys():
     v = _spk((1, 3, 130, 128), 0.5, 42)
     out = ops.spiking_attention(q, k, v, _lam(128, 43), 2)
     assert torch.count_nonzero(out).item() == 0
+
+
+def _pack(S):
+    """fp32 0 / 1 spikes [..., d] -> int32 words [..., d/32] (bit b of word w = channel 32w + b)."""
+    shifts = torch.arange(32, device=S.device, dtype=torch.int64)
+    words = (S.view(*S.shape[:-1], S.shape[-1] // 32, 32).long() << shifts).sum(-1)
+    return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+
+
+@pytest.mark.parametrize("shape,heads", [
+    ((4, 2, 256, 256), 4),     # dh = 64
+    ((2, 1, 100, 128), 4),     # dh = 32, ragged sequence length
+    ((1, 3, 130, 128), 8),     # dh = 16, a partial last tile
+    ((4, 8, 4096, 512), 8),    # the attention config's per-sample shape at B = 8
+])
+def test_packed_attention_matches_the_fp32_form(shape, heads):
+    """Attention over packed q, k, v gives the fp32-input attention's output bit
+    for bit (the kernels expand the words into the same staging values)."""
+    q, k, v = (_spk(shape, 0.15, s) for s in (11, 12, 13))
+    lam = _lam(shape[-1], 14)
+    want = ops.spiking_attention(q, k, v, lam, heads)
+    got = ops.spiking_attention_bits(_pack(q), _pack(k), _pack(v), lam, heads)
+    assert torch.equal(ops.unpack_spikes(_pack(q), shape[-1]), q)
+    assert torch.equal(got, want)

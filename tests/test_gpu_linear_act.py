@@ -102,16 +102,20 @@ def test_rejects_unsupported():
         ops.linear_act(x, w, b, act="relu")
 
 
+@pytest.mark.parametrize("act", ["heaviside", "vspike"])
 @pytest.mark.parametrize("R,K,N", [(1000, 512, 2048), (4097, 64, 96), (300, 256, 160)])
-def test_heaviside_bits_pack_the_heaviside_spikes(R, K, N):
-    """act="heaviside_bits" writes the same decisions as "heaviside", packed one
-    bit each (bit b of word w = column 32w + b), partial row tiles included."""
+def test_packed_epilogues_pack_the_spikes(R, K, N, act):
+    """act="heaviside_bits" / "vspike_bits" write the same decisions as
+    "heaviside" / "vspike", packed one bit each (bit b of word w = column
+    32w + b), partial row tiles included."""
     g = torch.Generator(device="cuda").manual_seed(R + N)
     x = torch.randn(R, K, generator=g, device="cuda")
     w = torch.randn(N, K, generator=g, device="cuda") / K ** 0.5
     b = torch.randn(N, generator=g, device="cuda") * 0.1
-    spikes = ops.linear_act(x, w, b, act="heaviside", thr=0.05)
-    bits = ops.linear_act(x, w, b, act="heaviside_bits", thr=0.05)
+    thr = 0.05 if act == "heaviside" else 0.5
+    spikes = ops.linear_act(x, w, b, act=act, thr=thr)
+    bits = ops.linear_act(x, w, b, act=act + "_bits", thr=thr)
+    assert 0.05 < float(spikes.mean()) < 0.95
     assert bits.dtype == torch.int32 and bits.shape == (R, N // 32)
     assert torch.equal(ops.unpack_spikes(bits, N), spikes)
 
