@@ -441,7 +441,8 @@ TF32_FLOP_PER_CLK_SM = 4096
 
 def run_linear(args, dist, cfg):
     """The C5 SpikingFFN fc1 with its threshold spike: act = (x W1^T + b - thr > 0)
-    over x [T*B*N, d] (ops.linear_act, three tf32 passes for fp32 accuracy)."""
+    over x [T*B*N, d] (ops.linear_act: a tf32 pass and a bf16 correction pass
+    over doubled K for fp32 accuracy, the tensor work of two tf32 passes)."""
     from spikestack_lite_b200 import _lib, ops
 
     dev = torch.device("cuda", dist.local)
@@ -487,7 +488,7 @@ def run_linear(args, dist, cfg):
     near = pre.abs() < 1e-5 * pre.abs().max()
     mism = int(((out[:256] > 0) != (pre > 0))[~near].sum().item())
     flops = 2.0 * R * K * N                      # the fp32 GEMM's FLOPs
-    tf32_work = 3 * flops                        # three tf32 passes
+    tf32_work = 2 * flops                        # tf32 pass + bf16 pass (2K at twice the rate)
     clk = clocks.summary().get("sm_mhz") or 1965.0
     peak_tf32 = TF32_FLOP_PER_CLK_SM * 148 * clk * 1e6 / 1e12
     ach = tf32_work / (kms / 1e3) / 1e12
@@ -778,7 +779,9 @@ def model_roofline(prof, tl, mc):
     pk = peaks()
     tot, n = prof["dense"]
     flops = tl.flops()  # algorithmic: 2*rows*K*N of every contraction in one chunk forward
-    passes = sum((3.0 if op == "linear_act" else 2.0) * 2.0 * r * k * nn for op, r, k, nn in tl.calls)
+    # tensor-core work in tf32-pass equivalents: the linear op issues one tf32 pass and one bf16
+    # correction pass over twice the K at twice the rate (= one tf32 pass), spike-linear two tf32 passes
+    passes = sum(2.0 * 2.0 * r * k * nn for op, r, k, nn in tl.calls)
     peak = pk["bf16_tflops_sustained"] / 2.0
     ach = flops / (tot / 1e3) / 1e12 if tot else None
     other = {k: round(v[0], 3) for k, v in prof.items()}
@@ -791,8 +794,9 @@ def model_roofline(prof, tl, mc):
                      "peak_src": f"{pk['src']} bf16 sustained {pk['bf16_tflops_sustained']} TFLOP/s / 2 "
                                  "(the tf32 dense rate is half the bf16 rate)",
                      "tf32_pass_frac": round(passes / (tot / 1e3) / 1e12 / peak, 4) if tot else None,
-                     "note": "achieved counts each fp32 GEMM's 2*rows*K*N once; the kernel issues 3 tf32 passes "
-                             "(linear op) or 2 (spike-linear) for fp32 accuracy, tf32_pass_frac counts them"},
+                     "note": "achieved counts each fp32 GEMM's 2*rows*K*N once; for fp32 accuracy the kernel "
+                             "issues the work of 2 tf32 passes (linear op: a tf32 pass plus a bf16 correction pass "
+                             "over doubled K; spike-linear: tf32 hi and lo), tf32_pass_frac counts them"},
         "kernel_ms_per_chunk": other,
     }
 

@@ -93,6 +93,12 @@ __host__ __device__ __forceinline__ uint32_t sw128_chunk(uint32_t r, uint32_t c)
   return r * 128u + (((c ^ (r & 7u)) & 7u) << 4);
 }
 
+// Four fp32 values rounded to bf16 (nearest even), packed in memory order.
+__device__ __forceinline__ uint2 bf16x4(float a, float b, float c, float d) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
 // ---------------------------------------------------------------- converters
 // Converter warps of the tf32 dense kernels (both operand orders share the
 // staging layout: 128 rows x 64 fp32 per slot, two 128-byte-swizzled atom
@@ -522,13 +528,18 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
   }
 }
 
-// Weight image for the tf32 kernel: for N-tile t and 64-wide K-chunk c,
+// Weight image for the tf32 kernels: for N-tile t and 64-wide K-chunk c,
 // [hi atom 0 | hi atom 1 | lo atom 0 | lo atom 1], each NT rows x 32 tf32 in
-// the 128-byte-swizzled K-major layout (one bulk copy per chunk).  Also
-// clears `zero_words` words at `zero` (the CSR pass state of the same call).
+// the 128-byte-swizzled K-major layout (one bulk copy per chunk), hi =
+// rna_tf32(w), lo = rna_tf32(w - hi).  A second region at img_b16 holds the
+// bf16 operand of the linear op's correction pass: per (t, c) [bf16(w - hi)
+// k0..63 | bf16(hi) k0..63], NT rows x 64 bf16 each in the same swizzle (hi
+// of a non-finite w is 0 there: the tf32 pass carries it).  Also clears
+// `zero_words` words at `zero` (the CSR pass state of the same call).
 template <typename WT>
 __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk,
-                                    unsigned char* img, uint32_t* zero, int64_t zero_words) {
+                                    unsigned char* img, unsigned char* img_b16, uint32_t* zero,
+                                    int64_t zero_words) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t npad = (int64_t)((N + NT - 1) / NT) * NT;
   const int64_t total = npad * nk * 16;  // one thread per (n, 4 k); n fastest: coalesced along W rows
@@ -541,24 +552,34 @@ __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, 
     const int64_t kq = i / npad;         // global 4-column group
     const int kc = (int)(kq / 16), k4 = (int)(kq % 16);
     const int t = (int)(ng / NT), nl = (int)(ng % NT);
-    float h[4], l[4];
+    float h[4], l[4], r[4], hb[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int k = kc * 64 + k4 * 4 + e;
       float x = 0.0f;
       if (k < K && ng < N) x = static_cast<float>(W[(int64_t)k * sk + ng * sn]);
       h[e] = tf32_rna(x);
-      l[e] = isfinite(x) ? tf32_rna(x - h[e]) : 0.0f;
+      const bool fin = isfinite(x);
+      r[e] = fin ? x - h[e] : 0.0f;  // exact in fp32
+      l[e] = tf32_rna(r[e]);
+      hb[e] = fin ? h[e] : 0.0f;
     }
     unsigned char* blk = img + ((size_t)t * nk + kc) * 4 * atom;
     const uint32_t off = (uint32_t)((k4 >> 3) * atom) + sw128_chunk((uint32_t)nl, (uint32_t)(k4 & 7));
     *reinterpret_cast<float4*>(blk + off) = make_float4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<float4*>(blk + 2 * atom + off) = make_float4(l[0], l[1], l[2], l[3]);
+    // bf16: columns 4 k4 .. 4 k4 + 3 are the half chunk (k4 & 1) of 16-byte chunk k4 >> 1
+    unsigned char* b16 = img_b16 + ((size_t)t * nk + kc) * 2 * atom;
+    const uint32_t off16 = sw128_chunk((uint32_t)nl, (uint32_t)(k4 >> 1)) + (uint32_t)(k4 & 1) * 8u;
+    *reinterpret_cast<uint2*>(b16 + off16) = bf16x4(r[0], r[1], r[2], r[3]);
+    *reinterpret_cast<uint2*>(b16 + atom + off16) = bf16x4(hb[0], hb[1], hb[2], hb[3]);
   }
 }
 
 // ---------------------------------------------------------------- host side
-inline size_t tf32_img_bytes(const TcPlan& p) { return (size_t)p.n_tiles * p.nk * p.NT * 512; }
+// The tf32 region (hi and lo, 4 atoms per tile and chunk), then the bf16 region (2 atoms).
+inline size_t tf32_img_region_bytes(const TcPlan& p) { return (size_t)p.n_tiles * p.nk * p.NT * 512; }
+inline size_t tf32_img_bytes(const TcPlan& p) { return tf32_img_region_bytes(p) + (size_t)p.n_tiles * p.nk * p.NT * 256; }
 
 template <int NT>
 int launch_tf32_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t stream) {
@@ -585,7 +606,7 @@ int launch_w_image_tf32(const void* W, int64_t sk, int64_t sn, int K, int N, con
   const int blocks = (int)min64(ceil_div(max64(total, zero_words), threads), 8192);
   prof_before(SPK_KERNEL_W_IMAGE, stream);
   w_image_tf32_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float*>(W), sk, sn, K, N, p.NT, p.nk,
-                                                             img, zero, zero_words);
+                                                             img, img + tf32_img_region_bytes(p), zero, zero_words);
   prof_after(SPK_KERNEL_W_IMAGE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);

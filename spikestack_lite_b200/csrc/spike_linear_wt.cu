@@ -12,6 +12,14 @@
 // negative, Inf/NaN) take the same hi pass / lo pass in place as in the
 // S-as-A kernel (spike_linear_tf32.cu), with the converter warps shared.
 //
+// The linear-activation op (general fp32 X) computes W X as one tf32 pass
+// w_hi * x_t (x_t = x truncated to tf32 by the tensor core) plus one bf16
+// pass over a doubled K: bf16(w - w_hi) * bf16(x) + bf16(w_hi) * bf16(x - x_t).
+// The bf16 pass costs the tensor core what one tf32 pass does (twice the
+// rate, twice the K), so two pass-times instead of the three of a 3xTF32
+// split; each product is within ~2^-18 of w x relative (~1e-6 of max |y| in
+// the tests), the dropped (w - w_hi)(x - x_t) is below 2^-21.
+//
 // Why this operand order: the S-as-A kernel keeps two 64 KB weight chunks in
 // shared memory for the whole time the MMAs read them, leaving room for three
 // 32 KB S slots, too few to cover the DRAM latency of a slot.  Here a weight
@@ -19,8 +27,10 @@
 // TMEM by four warps), so five S slots fit.
 //
 // TMEM (512 columns): [0, 256) two weight chunks, each [hi k0..63 | lo k0..63]
-// (one tf32 per column, lane = output column n); [256, 512) the accumulators
-// of a group of two row tiles (column = row, lane = n), single-buffered.
+// (one tf32 per column, lane = output column n; for the linear op the lo half
+// holds the 128 bf16 [w - w_hi | w_hi] of the correction pass, two per
+// column); [256, 512) the accumulators of a group of two row tiles (column =
+// row, lane = n), single-buffered.
 //
 // Warp roles (736 threads): warp 0 S producer (TMA, boxes of 32 columns x 32
 // rows), warp 1 TMEM owner + MMA issuer, warp 2 weight-piece producer (1-D
@@ -52,13 +62,14 @@ constexpr int kTmemCols = 512;
 constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 columns
 constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
 // Shared-memory rings per mode.  Spike-linear: five S slots.  Linear op:
-// three X slots and two remainder buffers (the X slot itself is the hi part).
+// three X slots and two bf16 correction-operand buffers (the X slot itself is
+// the tf32 pass's operand).
 // The GSMC recurrence (kXchg) gives one S slot to the epilogue's 16 KB gate
 // exchange buffer.
 template <bool kRelu, bool kXchg = false>
 struct Ring {
   static constexpr int NS = kRelu ? (kXchg ? 4 : 5) : 3;  // staging slots
-  static constexpr int NL = kRelu ? 0 : 2;  // remainder buffers
+  static constexpr int NL = kRelu ? 0 : 2;  // correction-operand buffers (linear op)
   static constexpr size_t kXchgBytes = kXchg ? 2 * 4 * 16 * 32 * sizeof(float) : 0;  // [2][4 gates][16 rows][32]
   static constexpr size_t kRing = (size_t)(NS + NL) * kStgBytes + (size_t)kNP * kPieceBytes + kXchgBytes;
   // barriers, lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
@@ -85,6 +96,17 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 with A = B = bf16 (K = 16).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Epilogue of the weights-in-TMEM kernel, per element y = D + bias[n].
 enum WtEpilogue : int {
   kEpiLinear = 0,     // y
@@ -103,11 +125,12 @@ __device__ __forceinline__ float wt_epilogue(float y, float thr) {
 }
 
 // Converter warps of the linear op.  The tensor core reads the X slot's fp32
-// values truncated to tf32 (the hi part); each warp reads its 8 rows once and
-// writes their remainders x - trunc(x) (exact in fp32; ~2^-21 relative after
-// the tensor core truncates them in turn) into a remainder buffer of the same
-// layout.  The slot itself is never rewritten, so a warp never waits for the
-// MMAs inside a slot, only for a free remainder buffer.
+// values truncated to tf32 (the hi part, x_t); each warp reads its 8 rows once
+// and writes the B operand of the correction pass into a buffer of the same
+// size: per row [bf16(x) k0..63 | bf16(x - x_t) k0..63] in the 128-byte
+// swizzle (x - x_t is exact in fp32; non-finite x gives 0 in both: the tf32
+// pass carries it).  The slot itself is never rewritten, so a warp never
+// waits for the MMAs inside a slot, only for a free buffer.
 template <int NS, int NL, int G>
 __device__ __forceinline__ void linear_converter(const int cw, const int lane, unsigned char* stg,
                                                  unsigned char* lob, uint64_t* stg_full, uint64_t* stg_empty,
@@ -117,16 +140,22 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
   constexpr int RPW = wt::kRows / wt::kConvWarps;  // rows per converter warp
   constexpr int NLD = RPW / 2;                      // 16-byte loads per lane and slot
   const int half = lane >> 4, cl = lane & 15;
-  uint32_t soff[NLD];
+  uint32_t soff[NLD], boff[NLD];
   int rls[NLD];
 #pragma unroll
   for (int i = 0; i < NLD; ++i) {
     rls[i] = cw * RPW + 2 * i + half;
+    // fp32 chunk cl holds columns 4cl .. 4cl+3: in bf16 half (cl & 1) of 16-byte chunk cl >> 1
     soff[i] = (uint32_t)((cl >> 3) * wt::kAtomBytes) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
+    boff[i] = sw128_chunk((uint32_t)rls[i], (uint32_t)(cl >> 1)) + (uint32_t)(cl & 1) * 8u;
   }
+  auto xv = [](uint32_t b) -> float {
+    const float x = __uint_as_float(b);
+    return isfinite(x) ? x : 0.0f;
+  };
   auto rem = [](uint32_t b) -> float {
     const float x = __uint_as_float(b);
-    return isinf(x) ? 0.0f : x - __uint_as_float(b & 0xffffe000u);  // NaN stays NaN
+    return isfinite(x) ? x - __uint_as_float(b & 0xffffe000u) : 0.0f;
   };
   int j = 0;
   bool ok = true;
@@ -139,16 +168,20 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
         if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(pg * G + t) * wt::kRows));
         const unsigned char* st = stg + s * wt::kStgBytes;
-        float4 lo[NLD];
+        uint2 xb[NLD], lo[NLD];
 #pragma unroll
         for (int i = 0; i < NLD; ++i) {
           const uint4 b = rls[i] < nrows ? *reinterpret_cast<const uint4*>(st + soff[i]) : make_uint4(0u, 0u, 0u, 0u);
-          lo[i] = make_float4(rem(b.x), rem(b.y), rem(b.z), rem(b.w));
+          xb[i] = bf16x4(xv(b.x), xv(b.y), xv(b.z), xv(b.w));
+          lo[i] = bf16x4(rem(b.x), rem(b.y), rem(b.z), rem(b.w));
         }
         if (j >= NL && !(ok = mbar_wait(&loe[l], ((j / NL) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         unsigned char* lb = lob + l * wt::kStgBytes;
 #pragma unroll
-        for (int i = 0; i < NLD; ++i) *reinterpret_cast<float4*>(lb + soff[i]) = lo[i];
+        for (int i = 0; i < NLD; ++i) {
+          *reinterpret_cast<uint2*>(lb + boff[i]) = xb[i];
+          *reinterpret_cast<uint2*>(lb + wt::kAtomBytes + boff[i]) = lo[i];
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -219,7 +252,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
-  unsigned char* lob = stg + NS * wt::kStgBytes;              // [NL][32 KB] remainders (linear op)
+  unsigned char* lob = stg + NS * wt::kStgBytes;              // [NL][32 KB] bf16 correction operand (linear op)
   unsigned char* pcs = lob + NL * wt::kStgBytes;              // [NP][16 KB] weight pieces
   float* xbuf = reinterpret_cast<float*>(pcs + NP * wt::kPieceBytes);  // GSMC gate exchange (kXchgBytes)
   uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes + RG::kXchgBytes);
@@ -235,8 +268,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
-  uint64_t* lof = drain + 1;   // [NL] remainder buffer written (linear op)
-  uint64_t* loe = lof + NL;    // [NL] remainder buffer read by the MMAs
+  uint64_t* lof = drain + 1;   // [NL] correction buffer written (linear op)
+  uint64_t* loe = lof + NL;    // [NL] correction buffer read by the MMAs
   static_assert(5 * NS + 2 * NP + 7 + 2 * NL == RG::kBarsUsed, "the barriers above fill the barrier block");
   uint8_t* lo_flag = reinterpret_cast<uint8_t*>(bars + RG::kBars);  // [NS][CW] bytes, 16-byte aligned
   int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
@@ -345,6 +378,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_tf32_f32(wt::kLanes, wt::kRows);
+      constexpr uint32_t idesc_b16 = umma_idesc_bf16_f32(wt::kLanes, wt::kRows);
       int j = 0, ja = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
@@ -362,8 +396,10 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           for (int t = 0; t < tg; ++t) {
             const int s = j % NS;
             if constexpr (!kRelu) {
-              // linear op: hi = the slot as the tensor core reads it, lo = the
-              // remainder buffer; both passes back to back
+              // linear op: the tf32 pass w_hi * x_t (the slot as the tensor core reads it), then the
+              // bf16 correction pass over K = 128: [bf16(w - w_hi) | bf16(w_hi)] (TMEM columns
+              // a_lo .. a_lo + 63, two bf16 per column) times [bf16(x) | bf16(x - x_t)] (the
+              // converters' buffer).  Both passes step 32 bytes of a 128-byte row per MMA.
               const int l = j % NL;
               if (!(ok = mbar_wait(&lof[l], (j / NL) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
               tc_fence_after();
@@ -374,12 +410,11 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
               for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
                 const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
                 umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db0 + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-                umma_tf32_ts(d, a_lo + (uint32_t)kk * 8u, db0 + off, idesc, 1u);
               }
 #pragma unroll
-              for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
+              for (int kk = 0; kk < 2 * wt::kKChunk / 16; ++kk) {
                 const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
-                umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, dl0 + off, idesc, 1u);
+                umma_bf16_ts(d, a_lo + (uint32_t)kk * 8u, dl0 + off, idesc_b16, 1u);
               }
               umma_commit(&stg_empty[s]);
               umma_commit(&loe[l]);
@@ -431,16 +466,19 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     if (lane == 0) {
       int jp = 0;
       bool ok = true;
+      // pieces 0, 1: tf32 hi; 2, 3: tf32 lo (spike-linear) or the two bf16 atoms (linear op)
       const unsigned char* img = a.wimg + (size_t)n_tile * nk * wt::kPieces * wt::kPieceBytes;
+      const unsigned char* img16 = kRelu ? nullptr : a.wimg_b16 + (size_t)n_tile * nk * 2 * wt::kPieceBytes;
       for (int c = 0; c < groups * nk && ok; ++c) {
         const int kc = c % nk;
         for (int p = 0; p < wt::kPieces; ++p, ++jp) {
           const int sp = jp % NP;
           if (jp >= NP && !(ok = mbar_wait(&pc_empty[sp], ((jp / NP) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
             break;
+          const unsigned char* src = (kRelu || p < 2) ? img + ((size_t)kc * wt::kPieces + p) * wt::kPieceBytes
+                                                      : img16 + ((size_t)kc * 2 + (p - 2)) * wt::kPieceBytes;
           mbar_arrive_expect_tx(&pc_full[sp], wt::kPieceBytes);
-          bulk_g2s(pcs + (size_t)sp * wt::kPieceBytes, img + ((size_t)kc * wt::kPieces + p) * wt::kPieceBytes,
-                   wt::kPieceBytes, &pc_full[sp]);
+          bulk_g2s(pcs + (size_t)sp * wt::kPieceBytes, src, wt::kPieceBytes, &pc_full[sp]);
         }
       }
       for (int i = (jp > NP ? jp - NP : 0); i < jp; ++i)
@@ -581,7 +619,9 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 // ---------------------------------------------------------------- host side
 // The weight image is the tf32 kernel's (tf32_img_bytes, w_image_tf32_kernel)
 // with NT = 128: per N tile and K chunk the pieces hi k0-31 | hi k32-63 |
-// lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle.
+// lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle, and in
+// the bf16 region (a.wimg_b16) the linear op's pieces bf16(w - hi) k0-63 |
+// bf16(hi) k0-63 of the same size.
 template <int kEpi, bool kRelu, bool kBits = false>
 int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
   auto kern = spike_linear_wt_kernel<kEpi, kRelu, kBits>;
@@ -605,6 +645,7 @@ inline TcArgs wt_args(int64_t R, int K, int N, const TcPlan& p, const unsigned c
   a.nk = p.nk;
   a.KWP = 2 * p.nk;
   a.wimg = img;
+  a.wimg_b16 = img + tf32_img_region_bytes(p);
   a.bias = o.bias;
   a.Y = o.Y;
   a.y_vec = 0;

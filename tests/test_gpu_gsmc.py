@@ -37,17 +37,17 @@ def test_step_matches_reference_engine(ref_engine):
 @pytest.mark.parametrize("adaptive", [True, False])
 def test_step_vs_oracle(adaptive):
     gi, gr, wd, bias, m, s, heat = _state(500, 32, 2)
-    c = [t.cpu() for t in (gi, gr, wd, bias, m, s, heat)]
+    # The oracle runs in float64: the host's vectorised float32 exp/tanh differ
+    # between CPUs (one host put hundreds of float32 oracle states 1e-5 away),
+    # while the kernel's float32 result lies within ~4e-7 of the float64 one.
+    c = [t.cpu().double() for t in (gi, gr, wd, bias, m, s, heat)]
     out = ops.fused_gsmc_step(gi, gr, wd, bias, m, s, heat, 1.0, 4.0, adaptive, 0.8)
     s_new, m_new, h_new = O.gsmc_step(*c, 1.0, 4.0, adaptive, 0.8)
     flips = (out.cpu() != s_new).sum().item()
-    assert flips <= 2  # libm vs CUDA expf/tanhf may flip a spike sitting on the threshold
+    assert flips <= 2  # float32 rounding may flip a spike sitting on the threshold
     same = out.cpu() == s_new
-    # the oracle's exp/tanh are the host's (vectorised per CPU); one box gave a
-    # state value outside 1e-5 on an unflipped spike, so the same budget of two
-    # elements as for the spike flips applies (the step is bit-exact against the
-    # reference engine in test_step_matches_reference_engine)
-    assert int(((m.cpu()[same] - m_new[same]).abs() > 1e-5).sum()) <= 2
+    assert float((m.cpu().double()[same] - m_new[same]).abs().max()) < 2e-6
+    assert float((heat.cpu().double()[same] - h_new[same]).abs().max()) < 2e-6
 
 
 @pytest.mark.parametrize("pool", ["mean", "last"])
