@@ -35,7 +35,11 @@
 // Warp roles (736 threads): warp 0 S producer (TMA, boxes of 32 columns x 32
 // rows), warp 1 TMEM owner + MMA issuer, warp 2 weight-piece producer (1-D
 // bulk copies), warps 3-18 converters, warps 19-22 weight loaders (shared
-// memory piece -> tcgen05.st into TMEM) and epilogue (TMEM -> + bias -> Y).
+// memory piece -> tcgen05.st into TMEM).  The epilogue (TMEM -> + bias -> Y)
+// runs on the loader warps for spike-linear, and on the sixteen converter
+// warps for the linear op, whose correction pass leaves the tensor core less
+// work per row: the MMAs wait for the single-buffered accumulators to drain,
+// so the drain is spread over four warps per TMEM lane quarter.
 // Every wait is bounded (2 s) and reports SPK_DEV_PIPE_TIMEOUT; issued copies
 // and MMAs are drained and TMEM is freed on every exit.
 #include "tma.cuh"
@@ -124,19 +128,80 @@ __device__ __forceinline__ float wt_epilogue(float y, float thr) {
   return y;
 }
 
+// Epilogue share of one converter warp of the linear op: the group iterated
+// g-th (accumulators of its tg row tiles in TMEM columns kDcol + 16b for the
+// 16-row blocks b) once its MMAs have committed.  The four converter warps of
+// TMEM lane quarter q take every fourth block, so sixteen warps drain the
+// accumulators while the tensor core waits for them.
+template <int kEpi, int G>
+__device__ __forceinline__ bool linear_group_epilogue(const int cw, const int lane, const TcArgs& a, const uint32_t tmem,
+                                                      const int n0, const float bias_n, uint64_t* acc_full,
+                                                      uint64_t* acc_empty, volatile int* abort_flag,
+                                                      const int64_t r_begin, const int64_t r_end, const int g,
+                                                      const int groups, const int tiles) {
+  const int q = (cw + 3) & 3;  // warp 3 + cw may access TMEM lanes [32q, 32q + 32)
+  const int sq = cw >> 2;      // its rank among the quarter's four converter warps
+  if (!mbar_wait(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
+  tc_fence_after();
+  const int pg = groups - 1 - g;
+  const int tg = min(G, tiles - pg * G);
+  const int64_t grow0 = r_begin + (int64_t)(pg * G) * wt::kRows;  // the tiles lie back to back in rows and columns
+  const int nb = (int)ceil_div(min64((int64_t)tg * wt::kRows, r_end - grow0), 16);
+  const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + wt::kDcol;
+  const int n = n0 + q * 32 + lane;
+  for (int b = sq; b < nb; b += 4) {  // warp-uniform bounds
+    float v[16];
+    tmem_ld16(tacc + (uint32_t)(16 * b), v);
+    tmem_wait_ld();
+    tmem_reg_fence(v);
+    const int64_t rowb = grow0 + (int64_t)b * 16;
+    if constexpr (kEpi == kEpiHeavisideBits || kEpi == kEpiVSpikeBits) {
+      // one ballot per row gives the row's word of this warp's 32 columns (N % 32 == 0: a
+      // warp's columns are all in range or all out); lane jj stores row rowb + jj's word
+      if (n0 + q * 32 < a.N) {
+        uint32_t word = 0u;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const float spike =
+              wt_epilogue<kEpi == kEpiHeavisideBits ? kEpiHeaviside : kEpiVSpike>(v[jj] + bias_n, a.thr);
+          const uint32_t bal = __ballot_sync(0xffffffffu, spike > 0.0f);
+          if (lane == jj) word = bal;
+        }
+        const int NW = a.N / 32;
+        if (lane < 16 && rowb + lane < r_end)
+          reinterpret_cast<uint32_t*>(a.Y)[(rowb + lane) * NW + (n0 / 32 + q)] = word;
+      }
+    } else if (n < a.N) {
+      float* y = a.Y + rowb * a.N + n;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        if (rowb + jj < r_end) y[(int64_t)jj * a.N] = wt_epilogue<kEpi>(v[jj] + bias_n, a.thr);
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acc_empty);
+  return true;
+}
+
 // Converter warps of the linear op.  The tensor core reads the X slot's fp32
 // values truncated to tf32 (the hi part, x_t); each warp reads its 8 rows once
 // and writes the B operand of the correction pass into a buffer of the same
 // size: per row [bf16(x) k0..63 | bf16(x - x_t) k0..63] in the 128-byte
 // swizzle (x - x_t is exact in fp32; non-finite x gives 0 in both: the tf32
 // pass carries it).  The slot itself is never rewritten, so a warp never
-// waits for the MMAs inside a slot, only for a free buffer.
-template <int NS, int NL, int G>
+// waits for the MMAs inside a slot, only for a free buffer.  The converters
+// also run the epilogue: that of group g - 1 after the first NL slots of group
+// g (the ones the MMAs take first once the accumulators are free), the last
+// group's after its slots.
+template <int kEpi, int NS, int NL, int G>
 __device__ __forceinline__ void linear_converter(const int cw, const int lane, unsigned char* stg,
                                                  unsigned char* lob, uint64_t* stg_full, uint64_t* stg_empty,
-                                                 uint64_t* lof, uint64_t* loe, volatile int* abort_flag,
-                                                 const int64_t r_begin, const int64_t r_end, const int nk,
-                                                 const int groups, const int tiles) {
+                                                 uint64_t* lof, uint64_t* loe, uint64_t* acc_full,
+                                                 uint64_t* acc_empty, volatile int* abort_flag, const TcArgs& a,
+                                                 const uint32_t tmem, const int n0, const int64_t r_begin,
+                                                 const int64_t r_end, const int nk, const int groups,
+                                                 const int tiles) {
   constexpr int RPW = wt::kRows / wt::kConvWarps;  // rows per converter warp
   constexpr int NLD = RPW / 2;                      // 16-byte loads per lane and slot
   const int half = lane >> 4, cl = lane & 15;
@@ -157,13 +222,17 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
     const float x = __uint_as_float(b);
     return isfinite(x) ? x - __uint_as_float(b & 0xffffe000u) : 0.0f;
   };
+  const int n = n0 + ((cw + 3) & 3) * 32 + lane;
+  const float bias_n = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.0f;
   int j = 0;
   bool ok = true;
   for (int g = 0; g < groups && ok; ++g) {
     const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
+    const int trig = min(NL, nk * tg);  // slots of this group converted before the previous group's epilogue
+    int js = 0;  // slot index within the group
     for (int kc = 0; kc < nk && ok; ++kc) {
-      for (int t = 0; t < tg; ++t, ++j) {
+      for (int t = 0; t < tg; ++t, ++j, ++js) {
         const int s = j % NS, l = j % NL;
         if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(pg * G + t) * wt::kRows));
@@ -188,9 +257,16 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
           mbar_arrive(&lof[l]);
           mbar_arrive(&stg_empty[s]);  // this warp has read the slot
         }
+        if (g >= 1 && js + 1 == trig &&
+            !(ok = linear_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag,
+                                                  r_begin, r_end, g - 1, groups, tiles)))
+          break;
       }
     }
   }
+  if (ok && groups > 0)
+    linear_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin, r_end,
+                                   groups - 1, groups, tiles);
 }
 
 // Converter warps of the packed-spike input (kBits).  The spikes arrive as
@@ -302,7 +378,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       mbar_init(&a_empty[b], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, kRelu ? 4 : CW);  // the epilogue warps: loaders (spike-linear) or converters (linear op)
     mbar_init(drain, 1);
     for (int l = 0; l < NL; ++l) {
       mbar_init(&lof[l], CW);
@@ -486,8 +562,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     }
   } else if (warp < 3 + CW) {
     if constexpr (!kRelu) {
-      linear_converter<NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, abort_flag, r_begin, r_end,
-                                  nk, groups, tiles);
+      linear_converter<kEpi, NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, acc_full, acc_empty,
+                                        abort_flag, a, tmem, n0, r_begin, r_end, nk, groups, tiles);
     } else if constexpr (kBits) {
       bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, lo_flag, abort_flag, a.bits_in, a.K / 32, r_begin,
                             r_end, nk, groups, tiles);
@@ -535,9 +611,13 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       ++ja;
       return true;
     };
-    for (int g = 0; g < groups && ok; ++g) {
+    // linear op: the converters run the epilogue, the loaders only stream the weight chunks
+    if constexpr (!kRelu) {
+      while (ok && ja < total_chunks) ok = load_chunk();
+    }
+    for (int g = 0; g < groups && ok && kRelu; ++g) {
       const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
-    const int tg = min(G, tiles - pg * G);
+      const int tg = min(G, tiles - pg * G);
       // this group's chunks, then the next group's first two (their buffers
       // free up with this group's last MMAs), then this group's epilogue
       while (ok && ja < min(total_chunks, (g + 1) * nk + 2)) ok = load_chunk();
