@@ -780,8 +780,9 @@ def model_roofline(prof, tl, mc):
     tot, n = prof["dense"]
     flops = tl.flops()  # algorithmic: 2*rows*K*N of every contraction in one chunk forward
     # tensor-core work in tf32-pass equivalents: the linear op issues one tf32 pass and one bf16
-    # correction pass over twice the K at twice the rate (= one tf32 pass), spike-linear two tf32 passes
-    passes = sum(2.0 * 2.0 * r * k * nn for op, r, k, nn in tl.calls)
+    # correction pass over twice the K at twice the rate (= one tf32 pass), spike-linear on fp32
+    # spikes two tf32 passes, on packed spikes three bf16 passes (the three-way split of W) = 1.5
+    passes = sum((1.5 if op == "spike_linear_bits" else 2.0) * 2.0 * r * k * nn for op, r, k, nn in tl.calls)
     peak = pk["bf16_tflops_sustained"] / 2.0
     ach = flops / (tot / 1e3) / 1e12 if tot else None
     other = {k: round(v[0], 3) for k, v in prof.items()}
@@ -796,7 +797,8 @@ def model_roofline(prof, tl, mc):
                      "tf32_pass_frac": round(passes / (tot / 1e3) / 1e12 / peak, 4) if tot else None,
                      "note": "achieved counts each fp32 GEMM's 2*rows*K*N once; for fp32 accuracy the kernel "
                              "issues the work of 2 tf32 passes (linear op: a tf32 pass plus a bf16 correction pass "
-                             "over doubled K; spike-linear: tf32 hi and lo), tf32_pass_frac counts them"},
+                             "over doubled K; spike-linear on fp32 spikes: tf32 hi and lo) or 1.5 (packed spikes: "
+                             "three bf16 passes over the split of W), tf32_pass_frac counts them"},
         "kernel_ms_per_chunk": other,
     }
 

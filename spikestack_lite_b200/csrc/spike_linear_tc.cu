@@ -77,6 +77,7 @@ struct TcArgs {
   int K, N, nk, KWP;      // nk: 64-wide K chunks; KWP = 2*nk: planar bitmap words per row
   const unsigned char* wimg;
   const unsigned char* wimg_b16;  // the image's bf16 region (the linear op's correction pass), or null
+  const unsigned char* wimg_b16x3;  // the image's three-way bf16 split (the packed-spike kernel), or null
   const float* bias;
   float* Y;
   int y_vec;              // Y 16-byte aligned and N % 4 == 0

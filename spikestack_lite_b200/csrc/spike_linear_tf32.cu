@@ -534,12 +534,16 @@ __global__ void __launch_bounds__(t32::kThreads, 1)
 // rna_tf32(w), lo = rna_tf32(w - hi).  A second region at img_b16 holds the
 // bf16 operand of the linear op's correction pass: per (t, c) [bf16(w - hi)
 // k0..63 | bf16(hi) k0..63], NT rows x 64 bf16 each in the same swizzle (hi
-// of a non-finite w is 0 there: the tf32 pass carries it).  Also clears
-// `zero_words` words at `zero` (the CSR pass state of the same call).
+// of a non-finite w is 0 there: the tf32 pass carries it).  A third region at
+// img_b16x3 holds the packed-spike kernel's operand: per (t, c) [b1 k0..63 |
+// b2 k0..63 | b3 k0..63] with b1 = bf16(w), b2 = bf16(w - b1), b3 = bf16(w -
+// b1 - b2) (w to ~2^-24 relative; the remainders are exact in fp32; b2 = b3 =
+// 0 for non-finite w).  Also clears `zero_words` words at `zero` (the CSR
+// pass state of the same call).
 template <typename WT>
 __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, int N, int NT, int nk,
-                                    unsigned char* img, unsigned char* img_b16, uint32_t* zero,
-                                    int64_t zero_words) {
+                                    unsigned char* img, unsigned char* img_b16, unsigned char* img_b16x3,
+                                    uint32_t* zero, int64_t zero_words) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t npad = (int64_t)((N + NT - 1) / NT) * NT;
   const int64_t total = npad * nk * 16;  // one thread per (n, 4 k); n fastest: coalesced along W rows
@@ -552,7 +556,7 @@ __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, 
     const int64_t kq = i / npad;         // global 4-column group
     const int kc = (int)(kq / 16), k4 = (int)(kq % 16);
     const int t = (int)(ng / NT), nl = (int)(ng % NT);
-    float h[4], l[4], r[4], hb[4];
+    float h[4], l[4], r[4], hb[4], b1[4], b2[4], b3[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int k = kc * 64 + k4 * 4 + e;
@@ -563,6 +567,10 @@ __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, 
       r[e] = fin ? x - h[e] : 0.0f;  // exact in fp32
       l[e] = tf32_rna(r[e]);
       hb[e] = fin ? h[e] : 0.0f;
+      b1[e] = __bfloat162float(__float2bfloat16_rn(x));
+      const float r1 = fin ? x - b1[e] : 0.0f;  // exact in fp32
+      b2[e] = __bfloat162float(__float2bfloat16_rn(r1));
+      b3[e] = r1 - b2[e];                        // exact; rounded below
     }
     unsigned char* blk = img + ((size_t)t * nk + kc) * 4 * atom;
     const uint32_t off = (uint32_t)((k4 >> 3) * atom) + sw128_chunk((uint32_t)nl, (uint32_t)(k4 & 7));
@@ -573,13 +581,20 @@ __global__ void w_image_tf32_kernel(const WT* W, int64_t sk, int64_t sn, int K, 
     const uint32_t off16 = sw128_chunk((uint32_t)nl, (uint32_t)(k4 >> 1)) + (uint32_t)(k4 & 1) * 8u;
     *reinterpret_cast<uint2*>(b16 + off16) = bf16x4(r[0], r[1], r[2], r[3]);
     *reinterpret_cast<uint2*>(b16 + atom + off16) = bf16x4(hb[0], hb[1], hb[2], hb[3]);
+    unsigned char* b3x = img_b16x3 + ((size_t)t * nk + kc) * 3 * atom;
+    *reinterpret_cast<uint2*>(b3x + off16) = bf16x4(b1[0], b1[1], b1[2], b1[3]);
+    *reinterpret_cast<uint2*>(b3x + atom + off16) = bf16x4(b2[0], b2[1], b2[2], b2[3]);
+    *reinterpret_cast<uint2*>(b3x + 2 * atom + off16) = bf16x4(b3[0], b3[1], b3[2], b3[3]);
   }
 }
 
 // ---------------------------------------------------------------- host side
-// The tf32 region (hi and lo, 4 atoms per tile and chunk), then the bf16 region (2 atoms).
+// The tf32 region (hi and lo, 4 atoms per tile and chunk), the bf16 region of
+// the linear op's correction pass (2 atoms), the three-way bf16 split (3 atoms).
 inline size_t tf32_img_region_bytes(const TcPlan& p) { return (size_t)p.n_tiles * p.nk * p.NT * 512; }
-inline size_t tf32_img_bytes(const TcPlan& p) { return tf32_img_region_bytes(p) + (size_t)p.n_tiles * p.nk * p.NT * 256; }
+inline size_t img_b16_region_bytes(const TcPlan& p) { return (size_t)p.n_tiles * p.nk * p.NT * 256; }
+inline size_t img_b16x3_offset(const TcPlan& p) { return tf32_img_region_bytes(p) + img_b16_region_bytes(p); }
+inline size_t tf32_img_bytes(const TcPlan& p) { return img_b16x3_offset(p) + (size_t)p.n_tiles * p.nk * p.NT * 384; }
 
 template <int NT>
 int launch_tf32_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t stream) {
@@ -606,7 +621,8 @@ int launch_w_image_tf32(const void* W, int64_t sk, int64_t sn, int K, int N, con
   const int blocks = (int)min64(ceil_div(max64(total, zero_words), threads), 8192);
   prof_before(SPK_KERNEL_W_IMAGE, stream);
   w_image_tf32_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float*>(W), sk, sn, K, N, p.NT, p.nk,
-                                                             img, img + tf32_img_region_bytes(p), zero, zero_words);
+                                                             img, img + tf32_img_region_bytes(p),
+                                                             img + img_b16x3_offset(p), zero, zero_words);
   prof_after(SPK_KERNEL_W_IMAGE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);

@@ -134,7 +134,7 @@ __device__ __forceinline__ float wt_epilogue(float y, float thr) {
 // TMEM lane quarter q take every fourth block, so sixteen warps drain the
 // accumulators while the tensor core waits for them.
 template <int kEpi, int G>
-__device__ __forceinline__ bool linear_group_epilogue(const int cw, const int lane, const TcArgs& a, const uint32_t tmem,
+__device__ __forceinline__ bool converter_group_epilogue(const int cw, const int lane, const TcArgs& a, const uint32_t tmem,
                                                       const int n0, const float bias_n, uint64_t* acc_full,
                                                       uint64_t* acc_empty, volatile int* abort_flag,
                                                       const int64_t r_begin, const int64_t r_end, const int g,
@@ -143,6 +143,9 @@ __device__ __forceinline__ bool linear_group_epilogue(const int cw, const int la
   const int sq = cw >> 2;      // its rank among the quarter's four converter warps
   if (!mbar_wait(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
   tc_fence_after();
+  // with a.early_s these warps skipped the dependency wait at the start; only the weight-image
+  // kernel can still be running then, and it never touches Y, but the first store waits anyway
+  if (a.early_s && g == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
   const int pg = groups - 1 - g;
   const int tg = min(G, tiles - pg * G);
   const int64_t grow0 = r_begin + (int64_t)(pg * G) * wt::kRows;  // the tiles lie back to back in rows and columns
@@ -258,63 +261,75 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
           mbar_arrive(&stg_empty[s]);  // this warp has read the slot
         }
         if (g >= 1 && js + 1 == trig &&
-            !(ok = linear_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag,
+            !(ok = converter_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag,
                                                   r_begin, r_end, g - 1, groups, tiles)))
           break;
       }
     }
   }
   if (ok && groups > 0)
-    linear_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin, r_end,
+    converter_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin, r_end,
                                    groups - 1, groups, tiles);
 }
 
 // Converter warps of the packed-spike input (kBits).  The spikes arrive as
 // 32-bit words, bit b of word w of a row = column 32w + b; each slot (128
-// rows x 64 columns = two words per row) is expanded into fp32 0 / 1 in the
-// K-major 128-byte swizzle of the B operand, exactly the values a TMA load of
-// the unpacked spikes would have put there.  Warp cw fills rows 8cw..8cw+7;
-// lane l takes row 8cw + l/4 and columns 16(l%4) .. +15 (four 16-byte
-// chunks).  The slot is free again when the MMAs that read it committed
-// (stg_empty), and ready for them when every converter arrived on chk.
+// rows x 64 columns = two words per row) is expanded into bf16 0 / 1 in the
+// K-major 128-byte swizzle of the B operand (one 16 KB atom column: the MMAs
+// multiply it by the three-way bf16 split of W).  Warp cw fills rows
+// 8cw..8cw+7; lane l takes row 8cw + l/4 and columns 16(l%4) .. +15 (two
+// 16-byte chunks; the 8 lanes of a quarter warp cover distinct bank groups).
+// The slot is free again when the MMAs that read it committed (stg_empty),
+// and ready for them when every converter arrived on chk.  The converters
+// also run the epilogue, as in the linear op.
 template <int NS, int G>
 __device__ __forceinline__ void bits_converter(const int cw, const int lane, unsigned char* stg, uint64_t* chk,
-                                               uint64_t* stg_empty, uint8_t* lo_flag, volatile int* abort_flag,
-                                               const uint32_t* bits, const int KW, const int64_t r_begin,
-                                               const int64_t r_end, const int nk, const int groups, const int tiles) {
+                                               uint64_t* stg_empty, uint64_t* acc_full, uint64_t* acc_empty,
+                                               volatile int* abort_flag, const TcArgs& a, const uint32_t tmem,
+                                               const int n0, const int64_t r_begin, const int64_t r_end,
+                                               const int nk, const int groups, const int tiles) {
   constexpr int CW = wt::kConvWarps;
+  const int KW = a.K / 32;
   const int rl = cw * (wt::kRows / CW) + (lane >> 2);  // row within the tile
   const int q = lane & 3;                               // 16-column group of the slot
-  const uint32_t abase = (uint32_t)((q >> 1) * wt::kAtomBytes);
+  const int n = n0 + ((cw + 3) & 3) * 32 + lane;
+  const float bias_n = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.0f;
+  auto bf16x4_bits = [](uint32_t nib) -> uint2 {  // 4 spikes -> bf16 1.0 (0x3f80) / 0
+    return make_uint2(((nib & 1u) ? 0x3f80u : 0u) | ((nib & 2u) ? 0x3f800000u : 0u),
+                      ((nib & 4u) ? 0x3f80u : 0u) | ((nib & 8u) ? 0x3f800000u : 0u));
+  };
   int j = 0;
   bool ok = true;
   for (int g = 0; g < groups && ok; ++g) {
     const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
+    const int trig = min(2, nk * tg);  // slots of this group converted before the previous group's epilogue
+    int js = 0;
     for (int kc = 0; kc < nk && ok; ++kc) {
-      for (int t = 0; t < tg; ++t, ++j) {
+      for (int t = 0; t < tg; ++t, ++j, ++js) {
         const int s = j % NS;
         if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         const int64_t row = r_begin + (int64_t)(pg * G + t) * wt::kRows + rl;
-        const uint32_t w = row < r_end ? bits[row * KW + 2 * kc + (q >> 1)] : 0u;
+        const uint32_t w = row < r_end ? a.bits_in[row * KW + 2 * kc + (q >> 1)] : 0u;
         const uint32_t h = (w >> ((q & 1) * 16)) & 0xffffu;
         unsigned char* st = stg + s * wt::kStgBytes;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const uint32_t nib = h >> (4 * c4);
-          const float4 f = make_float4((nib & 1u) ? 1.0f : 0.0f, (nib & 2u) ? 1.0f : 0.0f, (nib & 4u) ? 1.0f : 0.0f,
-                                       (nib & 8u) ? 1.0f : 0.0f);
-          *reinterpret_cast<float4*>(st + abase + sw128_chunk((uint32_t)rl, (uint32_t)((q & 1) * 4 + c4))) = f;
-        }
+        const uint2 c0 = bf16x4_bits(h), c1 = bf16x4_bits(h >> 4), c2 = bf16x4_bits(h >> 8), c3 = bf16x4_bits(h >> 12);
+        *reinterpret_cast<uint4*>(st + sw128_chunk((uint32_t)rl, (uint32_t)(2 * q))) = make_uint4(c0.x, c0.y, c1.x, c1.y);
+        *reinterpret_cast<uint4*>(st + sw128_chunk((uint32_t)rl, (uint32_t)(2 * q + 1))) =
+            make_uint4(c2.x, c2.y, c3.x, c3.y);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          lo_flag[s * CW + cw] = 0;  // exact: no lo pass
-          mbar_arrive(&chk[s]);
-        }
+        if (lane == 0) mbar_arrive(&chk[s]);
+        if (g >= 1 && js + 1 == trig &&
+            !(ok = converter_group_epilogue<kEpiLinear, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty,
+                                                           abort_flag, r_begin, r_end, g - 1, groups, tiles)))
+          break;
       }
     }
   }
+  if (ok && groups > 0)
+    converter_group_epilogue<kEpiLinear, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin,
+                                            r_end, groups - 1, groups, tiles);
 }
 
 // kRelu: spike-linear (relu'(S)); false: the linear-activation op (plain X).
@@ -325,6 +340,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
   using RG = wt::Ring<kRelu, kEpi == kEpiGsmc>;
   constexpr int G = wt::kG, NS = RG::NS, NL = RG::NL, NP = wt::kNP, CW = wt::kConvWarps;
+  constexpr int PPC = kBits ? 3 : wt::kPieces;  // weight pieces per K chunk
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   unsigned char* base = smem_aligned_1024(smem_dyn);
   unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
@@ -378,7 +394,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       mbar_init(&a_empty[b], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kRelu ? 4 : CW);  // the epilogue warps: loaders (spike-linear) or converters (linear op)
+    mbar_init(acc_empty, (kRelu && !kBits) ? 4 : CW);  // the epilogue warps: loaders or converters
     mbar_init(drain, 1);
     for (int l = 0; l < NL; ++l) {
       mbar_init(&lof[l], CW);
@@ -497,6 +513,24 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
               ++j;
               continue;
             }
+            if constexpr (kBits) {
+              // packed spikes: the slot holds bf16 0 / 1 (one 16 KB atom column); the chunk's
+              // TMEM columns a_hi + [0, 96) hold the three-way bf16 split b1 | b2 | b3 of W (two
+              // per column), so each 16-column step is three kind::f16 MMAs, exact per product
+              if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+              tc_fence_after();
+              const uint32_t d = tmem + wt::kDcol + (uint32_t)(t * wt::kRows);
+              const uint64_t db0 = umma_desc_sw128_kmajor(smem_u32(stg + s * wt::kStgBytes));
+#pragma unroll
+              for (int kk = 0; kk < wt::kKChunk / 16; ++kk)
+#pragma unroll
+                for (int p = 0; p < 3; ++p)
+                  umma_bf16_ts(d, a_hi + (uint32_t)(p * 32 + kk * 8), db0 + (uint64_t)(2 * kk), idesc_b16,
+                               (kc > 0 || kk > 0 || p > 0) ? 1u : 0u);
+              umma_commit(&stg_empty[s]);
+              ++j;
+              continue;
+            }
             if (!(ok = mbar_wait(&chk[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
             tc_fence_after();
             const uint4 lf = *reinterpret_cast<const uint4*>(lo_flag + s * CW);  // the 16 warps' flags
@@ -542,17 +576,20 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     if (lane == 0) {
       int jp = 0;
       bool ok = true;
-      // pieces 0, 1: tf32 hi; 2, 3: tf32 lo (spike-linear) or the two bf16 atoms (linear op)
+      // pieces 0, 1: tf32 hi; 2, 3: tf32 lo (spike-linear) or the two bf16 atoms (linear op);
+      // packed spikes: the three bf16 atoms b1, b2, b3
       const unsigned char* img = a.wimg + (size_t)n_tile * nk * wt::kPieces * wt::kPieceBytes;
       const unsigned char* img16 = kRelu ? nullptr : a.wimg_b16 + (size_t)n_tile * nk * 2 * wt::kPieceBytes;
+      const unsigned char* img3 = kBits ? a.wimg_b16x3 + (size_t)n_tile * nk * 3 * wt::kPieceBytes : nullptr;
       for (int c = 0; c < groups * nk && ok; ++c) {
         const int kc = c % nk;
-        for (int p = 0; p < wt::kPieces; ++p, ++jp) {
+        for (int p = 0; p < PPC; ++p, ++jp) {
           const int sp = jp % NP;
           if (jp >= NP && !(ok = mbar_wait(&pc_empty[sp], ((jp / NP) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
             break;
-          const unsigned char* src = (kRelu || p < 2) ? img + ((size_t)kc * wt::kPieces + p) * wt::kPieceBytes
-                                                      : img16 + ((size_t)kc * 2 + (p - 2)) * wt::kPieceBytes;
+          const unsigned char* src = kBits                ? img3 + ((size_t)kc * 3 + p) * wt::kPieceBytes
+                                     : (kRelu || p < 2) ? img + ((size_t)kc * wt::kPieces + p) * wt::kPieceBytes
+                                                        : img16 + ((size_t)kc * 2 + (p - 2)) * wt::kPieceBytes;
           mbar_arrive_expect_tx(&pc_full[sp], wt::kPieceBytes);
           bulk_g2s(pcs + (size_t)sp * wt::kPieceBytes, src, wt::kPieceBytes, &pc_full[sp]);
         }
@@ -565,7 +602,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       linear_converter<kEpi, NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, acc_full, acc_empty,
                                         abort_flag, a, tmem, n0, r_begin, r_end, nk, groups, tiles);
     } else if constexpr (kBits) {
-      bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, lo_flag, abort_flag, a.bits_in, a.K / 32, r_begin,
+      bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, acc_full, acc_empty, abort_flag, a, tmem, n0, r_begin,
                             r_end, nk, groups, tiles);
     } else {
       tf32_converter<NS, G, kRelu, true>(warp - 3, lane, stg, stg_full, chk, stg_empty, lo_go, lo_full, lo_flag, row_count,
@@ -587,7 +624,7 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       const int ab = ja & 1;
       if (ja >= 2 && !mbar_wait(&a_empty[ab], ((ja >> 1) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
       tc_fence_after();
-      for (int p = 0; p < wt::kPieces; ++p, ++jp) {
+      for (int p = 0; p < PPC; ++p, ++jp) {
         const int sp = jp % NP;
         if (!mbar_wait(&pc_full[sp], (jp / NP) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
         const unsigned char* src = pcs + (size_t)sp * wt::kPieceBytes;
@@ -611,11 +648,12 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       ++ja;
       return true;
     };
-    // linear op: the converters run the epilogue, the loaders only stream the weight chunks
-    if constexpr (!kRelu) {
+    // linear op and packed spikes: the converters run the epilogue, the loaders only stream the weight chunks
+    constexpr bool kConvEpi = !kRelu || kBits;
+    if constexpr (kConvEpi) {
       while (ok && ja < total_chunks) ok = load_chunk();
     }
-    for (int g = 0; g < groups && ok && kRelu; ++g) {
+    for (int g = 0; g < groups && ok && !kConvEpi; ++g) {
       const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
       const int tg = min(G, tiles - pg * G);
       // this group's chunks, then the next group's first two (their buffers
@@ -726,6 +764,7 @@ inline TcArgs wt_args(int64_t R, int K, int N, const TcPlan& p, const unsigned c
   a.KWP = 2 * p.nk;
   a.wimg = img;
   a.wimg_b16 = img + tf32_img_region_bytes(p);
+  a.wimg_b16x3 = img + img_b16x3_offset(p);
   a.bias = o.bias;
   a.Y = o.Y;
   a.y_vec = 0;

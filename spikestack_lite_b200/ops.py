@@ -262,7 +262,7 @@ def spike_linear_bits(bits, K, weight, bias=None):
     R = bits.numel() // bits.shape[-1]
     Y = torch.empty(*bits.shape[:-1], N, dtype=torch.float32, device=bits.device)
     lib = _lib.load()
-    _record("spike_linear", R, K, N)
+    _record("spike_linear_bits", R, K, N)
     img = _weight_image(weight, K, N, weight.stride(1), weight.stride(0), _lib.SPK_F32)
     ws, wsn = (None, 0) if img is not None else _lib.workspace(bits.device, lib.spk_linear_act_workspace_bytes(K, N))
     check(lib.spk_spike_linear_bits(ptr(bits), 1, R, K, ptr(weight), weight.stride(1), weight.stride(0), N, ptr(img),

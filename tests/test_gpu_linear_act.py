@@ -2,10 +2,11 @@
 
 The projections around the spike-linear path (SpikingFFN fc1 + threshold
 spike, attention q/k/v spikes, o_proj) are fp32 nn.Linear layers in the
-reference.  The engine computes them fp32-accurate (tf32 hi/lo splits of both
-operands): outputs within 1e-5 x max|ref| of the fp64 product, and no less
-accurate than the cuBLAS fp32 GEMM; spikes equal to the fp64 decision except
-where the pre-activation lies within rounding distance of the threshold."""
+reference.  The engine computes them to fp32-class accuracy (a tf32 pass
+w_hi * x_t plus a bf16 correction pass bf16(w - w_hi) * bf16(x) + bf16(w_hi) *
+bf16(x - x_t)): outputs within 1e-5 x max|ref| of the fp64 product (~1e-6 in
+practice); spikes equal to the fp64 decision except where the pre-activation
+lies within rounding distance of the threshold."""
 import pytest
 import torch
 
@@ -122,9 +123,11 @@ def test_packed_epilogues_pack_the_spikes(R, K, N, act):
 
 @pytest.mark.parametrize("T,M,K,N", [(4, 1000, 2048, 512), (2, 4097, 128, 96), (1, 129, 64, 200)])
 def test_spike_linear_bits_matches_the_unpacked_dense_branch(T, M, K, N):
-    """fc2 on packed spikes gives bit-identical output to the dense branch on
-    the unpacked fp32 spikes (the expanded staging slots hold the same values
-    a TMA load of them would)."""
+    """fc2 on packed spikes against the dense branch on the unpacked fp32
+    spikes and the float64 product.  The packed kernel multiplies bf16 0 / 1
+    by the three-way bf16 split of W (exact products, fp32 accumulation), the
+    dense branch by the tf32 hi + lo split (W to ~2^-22): both lie within fp32
+    accumulation error of the exact sum."""
     g = torch.Generator(device="cuda").manual_seed(T * M + K)
     S = (torch.rand(T, M, K, generator=g, device="cuda") < 0.5).float()
     shifts = torch.arange(32, device="cuda", dtype=torch.int64)
@@ -135,9 +138,11 @@ def test_spike_linear_bits_matches_the_unpacked_dense_branch(T, M, K, N):
     b = torch.randn(N, generator=g, device="cuda")
     y_bits = ops.spike_linear_bits(bits, K, w, b)
     y_dense = ops.spike_linear(S, weight=w, bias=b, branch="dense")
-    assert torch.equal(y_bits, y_dense)
     ref = S.cpu().double() @ w.cpu().double().t() + b.cpu().double()
-    assert float((y_bits.cpu().double() - ref).abs().max() / ref.abs().max()) < 1e-4
+    scale = float(ref.abs().max())
+    err_bits = float((y_bits.cpu().double() - ref).abs().max()) / scale
+    err_dense = float((y_dense.cpu().double() - ref).abs().max()) / scale
+    assert err_bits < 1e-5 and err_dense < 1e-5, (err_bits, err_dense)  # ~3e-6 at K = 2048
 
 
 def test_packed_paths_with_no_rows():
