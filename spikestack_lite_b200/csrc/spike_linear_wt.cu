@@ -65,17 +65,26 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kAcol = 0;               // weight chunk buffers: 2 x 128 columns
 constexpr uint32_t kDcol = 256;             // accumulators: kG x 128 columns
+// Rows of a 128-row tile that one CTA stages: all of them, or half in a CTA
+// pair (tcgen05 cta_group::2 splits the B operand by rows between the pair).
+template <bool kPair>
+struct Geo {
+  static constexpr int kRowsC = kPair ? kRows / 2 : kRows;
+  static constexpr int kAtom = kRowsC * 128;  // one swizzle-atom column of a slot
+  static constexpr int kStg = 2 * kAtom;      // a slot: 64 fp32 columns
+};
 // Shared-memory rings per mode.  Spike-linear: five S slots.  Linear op:
 // three X slots and two bf16 correction-operand buffers (the X slot itself is
-// the tf32 pass's operand).
-// The GSMC recurrence (kXchg) gives one S slot to the epilogue's 16 KB gate
-// exchange buffer.
-template <bool kRelu, bool kXchg = false>
+// the tf32 pass's operand); a CTA pair stages half-height slots, four and
+// three of them.  The GSMC recurrence (kXchg) gives one S slot to the
+// epilogue's 16 KB gate exchange buffer.
+template <bool kRelu, bool kXchg = false, bool kPair = false>
 struct Ring {
-  static constexpr int NS = kRelu ? (kXchg ? 4 : 5) : 3;  // staging slots
-  static constexpr int NL = kRelu ? 0 : 2;  // correction-operand buffers (linear op)
+  static constexpr int NS = kPair ? 4 : kRelu ? (kXchg ? 4 : 5) : 3;  // staging slots
+  static constexpr int NL = kPair ? 3 : kRelu ? 0 : 2;  // correction-operand buffers (linear op)
   static constexpr size_t kXchgBytes = kXchg ? 2 * 4 * 16 * 32 * sizeof(float) : 0;  // [2][4 gates][16 rows][32]
-  static constexpr size_t kRing = (size_t)(NS + NL) * kStgBytes + (size_t)kNP * kPieceBytes + kXchgBytes;
+  static constexpr size_t kRing =
+      (size_t)(NS + NL) * Geo<kPair>::kStg + (size_t)kNP * kPieceBytes + kXchgBytes;
   // barriers, lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
   static constexpr int kBarsUsed = 5 * NS + 2 * NL + 2 * kNP + 7;
   static constexpr int kBars = kBarsUsed + (kBarsUsed & 1);  // even: the lo flags after them stay 16-byte aligned
@@ -111,6 +120,32 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// The same for a CTA pair (cta_group::2, issued by CTA 0; M = 256 across the
+// pair's TMEM, B split by rows between their shared memories), with an
+// all-zero disable-output-lane mask.
+__device__ __forceinline__ void umma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u)
+      : "memory");
+}
+
 // Epilogue of the weights-in-TMEM kernel, per element y = D + bias[n].
 enum WtEpilogue : int {
   kEpiLinear = 0,     // y
@@ -133,7 +168,7 @@ __device__ __forceinline__ float wt_epilogue(float y, float thr) {
 // 16-row blocks b) once its MMAs have committed.  The four converter warps of
 // TMEM lane quarter q take every fourth block, so sixteen warps drain the
 // accumulators while the tensor core waits for them.
-template <int kEpi, int G>
+template <int kEpi, int G, bool kPair = false>
 __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int lane, const TcArgs& a, const uint32_t tmem,
                                                       const int n0, const float bias_n, uint64_t* acc_full,
                                                       uint64_t* acc_empty, volatile int* abort_flag,
@@ -141,7 +176,7 @@ __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int
                                                       const int groups, const int tiles) {
   const int q = (cw + 3) & 3;  // warp 3 + cw may access TMEM lanes [32q, 32q + 32)
   const int sq = cw >> 2;      // its rank among the quarter's four converter warps
-  if (!mbar_wait(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
+  if (!mbar_wait<kPair>(acc_full, g & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
   tc_fence_after();
   // with a.early_s these warps skipped the dependency wait at the start; only the weight-image
   // kernel can still be running then, and it never touches Y, but the first store waits anyway
@@ -183,7 +218,10 @@ __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int
   }
   tc_fence_before();
   __syncwarp();
-  if (lane == 0) mbar_arrive(acc_empty);
+  if (lane == 0) {
+    if constexpr (kPair) mbar_arrive_rank0(acc_empty);  // the pair's MMAs wait on CTA 0's barrier
+    else mbar_arrive(acc_empty);
+  }
   return true;
 }
 
@@ -197,15 +235,16 @@ __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int
 // also run the epilogue: that of group g - 1 after the first NL slots of group
 // g (the ones the MMAs take first once the accumulators are free), the last
 // group's after its slots.
-template <int kEpi, int NS, int NL, int G>
+template <int kEpi, int NS, int NL, int G, bool kPair = false>
 __device__ __forceinline__ void linear_converter(const int cw, const int lane, unsigned char* stg,
                                                  unsigned char* lob, uint64_t* stg_full, uint64_t* stg_empty,
                                                  uint64_t* lof, uint64_t* loe, uint64_t* acc_full,
                                                  uint64_t* acc_empty, volatile int* abort_flag, const TcArgs& a,
                                                  const uint32_t tmem, const int n0, const int64_t r_begin,
                                                  const int64_t r_end, const int nk, const int groups,
-                                                 const int tiles) {
-  constexpr int RPW = wt::kRows / wt::kConvWarps;  // rows per converter warp
+                                                 const int tiles, const int rank) {
+  using GE = wt::Geo<kPair>;
+  constexpr int RPW = GE::kRowsC / wt::kConvWarps;  // rows per converter warp
   constexpr int NLD = RPW / 2;                      // 16-byte loads per lane and slot
   const int half = lane >> 4, cl = lane & 15;
   uint32_t soff[NLD], boff[NLD];
@@ -214,7 +253,7 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
   for (int i = 0; i < NLD; ++i) {
     rls[i] = cw * RPW + 2 * i + half;
     // fp32 chunk cl holds columns 4cl .. 4cl+3: in bf16 half (cl & 1) of 16-byte chunk cl >> 1
-    soff[i] = (uint32_t)((cl >> 3) * wt::kAtomBytes) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
+    soff[i] = (uint32_t)((cl >> 3) * GE::kAtom) + sw128_chunk((uint32_t)rls[i], (uint32_t)(cl & 7));
     boff[i] = sw128_chunk((uint32_t)rls[i], (uint32_t)(cl >> 1)) + (uint32_t)(cl & 1) * 8u;
   }
   auto xv = [](uint32_t b) -> float {
@@ -232,14 +271,18 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
   for (int g = 0; g < groups && ok; ++g) {
     const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
-    const int trig = min(NL, nk * tg);  // slots of this group converted before the previous group's epilogue
+    // slots of this group converted before the previous group's epilogue: at most NS (converting
+    // slot NS + 1 would need a slot that only this group's MMAs free, which wait for the epilogue)
+    const int trig = min(min(NL, NS), nk * tg);
     int js = 0;  // slot index within the group
     for (int kc = 0; kc < nk && ok; ++kc) {
       for (int t = 0; t < tg; ++t, ++j, ++js) {
         const int s = j % NS, l = j % NL;
-        if (!(ok = mbar_wait(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        const int nrows = (int)min64(wt::kRows, r_end - (r_begin + (int64_t)(pg * G + t) * wt::kRows));
-        const unsigned char* st = stg + s * wt::kStgBytes;
+        if (!(ok = mbar_wait<kPair>(&stg_full[s], (j / NS) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        // rows of this CTA's part of the tile (the second CTA of a pair stages rows 64 .. 127)
+        const int nrows = (int)min64(
+            GE::kRowsC, r_end - (r_begin + (int64_t)(pg * G + t) * wt::kRows + (int64_t)rank * GE::kRowsC));
+        const unsigned char* st = stg + s * GE::kStg;
         uint2 xb[NLD], lo[NLD];
 #pragma unroll
         for (int i = 0; i < NLD; ++i) {
@@ -247,28 +290,29 @@ __device__ __forceinline__ void linear_converter(const int cw, const int lane, u
           xb[i] = bf16x4(xv(b.x), xv(b.y), xv(b.z), xv(b.w));
           lo[i] = bf16x4(rem(b.x), rem(b.y), rem(b.z), rem(b.w));
         }
-        if (j >= NL && !(ok = mbar_wait(&loe[l], ((j / NL) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        unsigned char* lb = lob + l * wt::kStgBytes;
+        if (j >= NL && !(ok = mbar_wait<kPair>(&loe[l], ((j / NL) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        unsigned char* lb = lob + l * GE::kStg;
 #pragma unroll
         for (int i = 0; i < NLD; ++i) {
           *reinterpret_cast<uint2*>(lb + boff[i]) = xb[i];
-          *reinterpret_cast<uint2*>(lb + wt::kAtomBytes + boff[i]) = lo[i];
+          *reinterpret_cast<uint2*>(lb + GE::kAtom + boff[i]) = lo[i];
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&lof[l]);
+          if constexpr (kPair) mbar_arrive_rank0(&lof[l]);  // the pair's MMAs wait on CTA 0's barrier
+          else mbar_arrive(&lof[l]);
           mbar_arrive(&stg_empty[s]);  // this warp has read the slot
         }
         if (g >= 1 && js + 1 == trig &&
-            !(ok = converter_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag,
+            !(ok = converter_group_epilogue<kEpi, G, kPair>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag,
                                                   r_begin, r_end, g - 1, groups, tiles)))
           break;
       }
     }
   }
   if (ok && groups > 0)
-    converter_group_epilogue<kEpi, G>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin, r_end,
+    converter_group_epilogue<kEpi, G, kPair>(cw, lane, a, tmem, n0, bias_n, acc_full, acc_empty, abort_flag, r_begin, r_end,
                                    groups - 1, groups, tiles);
 }
 
@@ -303,7 +347,7 @@ __device__ __forceinline__ void bits_converter(const int cw, const int lane, uns
   for (int g = 0; g < groups && ok; ++g) {
     const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
-    const int trig = min(2, nk * tg);  // slots of this group converted before the previous group's epilogue
+    const int trig = min(min(2, NS), nk * tg);  // slots converted before the previous group's epilogue (<= NS)
     int js = 0;
     for (int kc = 0; kc < nk && ok; ++kc) {
       for (int t = 0; t < tg; ++t, ++j, ++js) {
@@ -334,18 +378,26 @@ __device__ __forceinline__ void bits_converter(const int cw, const int lane, uns
 
 // kRelu: spike-linear (relu'(S)); false: the linear-activation op (plain X).
 // kBits (with kRelu): the spikes come packed, 1 bit each (a.bits_in).
-template <int kEpi, bool kRelu, bool kBits = false>
+// kPair (linear op): launched in clusters of two CTAs along N, the pair's
+// MMAs run as tcgen05 cta_group::2 (M = 256: the two CTAs' 128-column weight
+// tiles in their TMEM; N = 128 rows: each CTA stages 64 of them), issued by
+// CTA 0; every barrier the MMAs wait on lives in CTA 0 and collects both
+// CTAs' arrivals, every MMA commit arrives in both CTAs.  Each SM then reads
+// half the B operand per FLOP and converts half the rows.
+template <int kEpi, bool kRelu, bool kBits = false, bool kPair = false>
 __global__ void __launch_bounds__(wt::kThreads, 1)
     spike_linear_wt_kernel(const __grid_constant__ CUtensorMap tmap_s, TcArgs a) {
-  if (gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
-  using RG = wt::Ring<kRelu, kEpi == kEpiGsmc>;
+  static_assert(!kPair || !kRelu, "CTA pairs: the linear op only");
+  if (!kPair && gated_off(a.gate, SPK_BRANCH_DENSE)) return;  // the automatic choice took the CSR branch
+  using RG = wt::Ring<kRelu, kEpi == kEpiGsmc, kPair>;
+  using GE = wt::Geo<kPair>;
   constexpr int G = wt::kG, NS = RG::NS, NL = RG::NL, NP = wt::kNP, CW = wt::kConvWarps;
   constexpr int PPC = kBits ? 3 : wt::kPieces;  // weight pieces per K chunk
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   unsigned char* base = smem_aligned_1024(smem_dyn);
-  unsigned char* stg = base;                                  // [NS][2 atoms x 16 KB] fp32 staging = B operand
-  unsigned char* lob = stg + NS * wt::kStgBytes;              // [NL][32 KB] bf16 correction operand (linear op)
-  unsigned char* pcs = lob + NL * wt::kStgBytes;              // [NP][16 KB] weight pieces
+  unsigned char* stg = base;                                  // [NS][2 atoms] fp32 staging = B operand
+  unsigned char* lob = stg + NS * GE::kStg;                   // [NL][2 atoms] bf16 correction operand (linear op)
+  unsigned char* pcs = lob + NL * GE::kStg;                   // [NP][16 KB] weight pieces
   float* xbuf = reinterpret_cast<float*>(pcs + NP * wt::kPieceBytes);  // GSMC gate exchange (kXchgBytes)
   uint64_t* bars = reinterpret_cast<uint64_t*>(pcs + NP * wt::kPieceBytes + RG::kXchgBytes);
   uint64_t* stg_full = bars;
@@ -369,9 +421,11 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r_begin = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int rank = kPair ? (int)cluster_ctarank() : 0;  // CTA 0 of a pair issues the MMAs
+  // a pair's grid is (N tiles, row ranges) with clusters of (2, 1, 1); otherwise (row ranges, N tiles)
+  const int64_t r_begin = (int64_t)(kPair ? blockIdx.y : blockIdx.x) * a.rows_per_cta;
   const int64_t r_end = min64(a.R, r_begin + a.rows_per_cta);
-  const int n_tile = blockIdx.y;
+  const int n_tile = kPair ? blockIdx.x : blockIdx.y;
   const int n0 = n_tile * wt::kLanes;
   const int nk = a.nk;
   const int tiles = r_end > r_begin ? (int)ceil_div(r_end - r_begin, wt::kRows) : 0;
@@ -389,26 +443,33 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       mbar_init(&pc_full[p], 1);
       mbar_init(&pc_empty[p], 4);
     }
+    constexpr int kCtas = kPair ? 2 : 1;  // CTAs arriving on the barriers the MMAs wait on
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&a_full[b], 4);
+      mbar_init(&a_full[b], 4 * kCtas);
       mbar_init(&a_empty[b], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, (kRelu && !kBits) ? 4 : CW);  // the epilogue warps: loaders or converters
+    mbar_init(acc_empty, (kRelu && !kBits) ? 4 : CW * kCtas);  // the epilogue warps: loaders or converters
     mbar_init(drain, 1);
     for (int l = 0; l < NL; ++l) {
-      mbar_init(&lof[l], CW);
+      mbar_init(&lof[l], CW * kCtas);
       mbar_init(&loe[l], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, wt::kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, wt::kTmemCols);  // warp 1 of both CTAs, the same slot offset
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, wt::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // Programmatic dependent of the kernel before it.  When that is the
@@ -426,16 +487,22 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     // (none for packed spikes: the converter warps build the slots)
     if (lane == 0 && !kBits) {
       tma_prefetch_map(&tmap_s);
-      auto load_s = [&](int s, int64_t row0, int kc) {
-        // 32-row boxes up to the tile's last valid row: no reads past the CTA's range
-        // (rows a box leaves out keep stale data; the converters and the epilogue ignore them)
-        const int nbox = (int)ceil_div(min64(wt::kRows, r_end - row0), wt::kBoxRows);
+      auto load_s = [&](int s, int64_t tile_row0, int kc) {
+        // this CTA's rows of the tile (a pair's second CTA stages rows 64 .. 127), in 32-row
+        // boxes up to the last valid row: no reads past the CTA's range (rows a box leaves out
+        // keep stale data; the converters and the epilogue ignore them)
+        const int64_t row0 = tile_row0 + (int64_t)rank * GE::kRowsC;
+        const int nbox = row0 < r_end ? (int)ceil_div(min64(GE::kRowsC, r_end - row0), wt::kBoxRows) : 0;
+        if (nbox == 0) {
+          mbar_arrive(&stg_full[s]);
+          return;
+        }
         mbar_arrive_expect_tx(&stg_full[s], (uint32_t)(2 * nbox * wt::kBoxBytes));
         for (int b = 0; b < nbox; ++b) {
-          unsigned char* dst = stg + s * wt::kStgBytes + b * wt::kBoxBytes;
+          unsigned char* dst = stg + s * GE::kStg + b * wt::kBoxBytes;
           const int y = (int)row0 + b * wt::kBoxRows;
           tma_load_2d(dst, &tmap_s, kc * wt::kKChunk, y, &stg_full[s]);
-          tma_load_2d(dst + wt::kAtomBytes, &tmap_s, kc * wt::kKChunk + 32, y, &stg_full[s]);
+          tma_load_2d(dst + GE::kAtom, &tmap_s, kc * wt::kKChunk + 32, y, &stg_full[s]);
         }
       };
       int pre = 0;  // slots requested before the wait: the first NS (or all), only when S is known complete
@@ -455,7 +522,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           for (int t = 0; t < tg; ++t, ++j) {
             if (j < pre) continue;
             const int s = j % NS;
-            if (j >= NS && !(ok = mbar_wait(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
+            if (j >= NS &&
+                !(ok = mbar_wait<kPair>(&stg_empty[s], ((j / NS) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)))
               break;
             load_s(s, r_begin + (int64_t)(pg * G + t) * wt::kRows, kc);
           }
@@ -468,20 +536,25 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_tf32_f32(wt::kLanes, wt::kRows);
-      constexpr uint32_t idesc_b16 = umma_idesc_bf16_f32(wt::kLanes, wt::kRows);
+    if (lane == 0 && rank == 0) {
+      constexpr int kM = kPair ? 2 * wt::kLanes : wt::kLanes;  // a pair: M = 256 over both CTAs' TMEM
+      constexpr uint32_t idesc = umma_idesc_tf32_f32(kM, wt::kRows);
+      constexpr uint32_t idesc_b16 = umma_idesc_bf16_f32(kM, wt::kRows);
+      auto commit = [](uint64_t* bar) {  // a pair's commits arrive in both CTAs
+        if constexpr (kPair) umma_commit_pair(bar);
+        else umma_commit(bar);
+      };
       int j = 0, ja = 0;
       bool ok = true;
       for (int g = 0; g < groups && ok; ++g) {
         const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
         // the accumulators are single-buffered: the previous group's epilogue has read them
-        if (g >= 1 && !(ok = mbar_wait(acc_empty, (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+        if (g >= 1 && !(ok = mbar_wait<kPair>(acc_empty, (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
         tc_fence_after();
         for (int kc = 0; kc < nk && ok; ++kc) {
           const int ab = ja & 1;
-          if (!(ok = mbar_wait(&a_full[ab], (ja >> 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+          if (!(ok = mbar_wait<kPair>(&a_full[ab], (ja >> 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
           tc_fence_after();
           const uint32_t a_hi = tmem + wt::kAcol + (uint32_t)ab * 128u;
           const uint32_t a_lo = a_hi + 64u;
@@ -493,23 +566,27 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
               // a_lo .. a_lo + 63, two bf16 per column) times [bf16(x) | bf16(x - x_t)] (the
               // converters' buffer).  Both passes step 32 bytes of a 128-byte row per MMA.
               const int l = j % NL;
-              if (!(ok = mbar_wait(&lof[l], (j / NL) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+              if (!(ok = mbar_wait<kPair>(&lof[l], (j / NL) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
               tc_fence_after();
               const uint32_t d = tmem + wt::kDcol + (uint32_t)(t * wt::kRows);
-              const uint64_t db0 = umma_desc_sw128_kmajor(smem_u32(stg + s * wt::kStgBytes));
-              const uint64_t dl0 = umma_desc_sw128_kmajor(smem_u32(lob + l * wt::kStgBytes));
+              // a pair: the same offsets in both CTAs' shared memory hold their halves of the rows
+              const uint64_t db0 = umma_desc_sw128_kmajor(smem_u32(stg + s * GE::kStg));
+              const uint64_t dl0 = umma_desc_sw128_kmajor(smem_u32(lob + l * GE::kStg));
 #pragma unroll
               for (int kk = 0; kk < wt::kKChunk / 8; ++kk) {
-                const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
-                umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db0 + off, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                const uint64_t off = (uint64_t)(((kk >> 2) * GE::kAtom + (kk & 3) * 32) >> 4);
+                const uint32_t acc = (kc > 0 || kk > 0) ? 1u : 0u;
+                if constexpr (kPair) umma_tf32_ts_pair(d, a_hi + (uint32_t)kk * 8u, db0 + off, idesc, acc);
+                else umma_tf32_ts(d, a_hi + (uint32_t)kk * 8u, db0 + off, idesc, acc);
               }
 #pragma unroll
               for (int kk = 0; kk < 2 * wt::kKChunk / 16; ++kk) {
-                const uint64_t off = (uint64_t)(((kk >> 2) * wt::kAtomBytes + (kk & 3) * 32) >> 4);
-                umma_bf16_ts(d, a_lo + (uint32_t)kk * 8u, dl0 + off, idesc_b16, 1u);
+                const uint64_t off = (uint64_t)(((kk >> 2) * GE::kAtom + (kk & 3) * 32) >> 4);
+                if constexpr (kPair) umma_bf16_ts_pair(d, a_lo + (uint32_t)kk * 8u, dl0 + off, idesc_b16, 1u);
+                else umma_bf16_ts(d, a_lo + (uint32_t)kk * 8u, dl0 + off, idesc_b16, 1u);
               }
-              umma_commit(&stg_empty[s]);
-              umma_commit(&loe[l]);
+              commit(&stg_empty[s]);
+              commit(&loe[l]);
               ++j;
               continue;
             }
@@ -561,14 +638,14 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
             ++j;
           }
           if (!ok) break;
-          umma_commit(&a_empty[ab]);
+          commit(&a_empty[ab]);
           ++ja;
         }
-        if (ok) umma_commit(acc_full);
+        if (ok) commit(acc_full);
       }
       if (!ok) {  // issued MMAs finish before TMEM and shared memory are released
-        umma_commit(drain);
-        mbar_wait(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);
+        commit(drain);
+        mbar_wait<kPair>(drain, 0, nullptr, SPK_DEV_PIPE_TIMEOUT);
       }
     }
   } else if (warp == 2) {
@@ -599,8 +676,9 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     }
   } else if (warp < 3 + CW) {
     if constexpr (!kRelu) {
-      linear_converter<kEpi, NS, NL, G>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, acc_full, acc_empty,
-                                        abort_flag, a, tmem, n0, r_begin, r_end, nk, groups, tiles);
+      linear_converter<kEpi, NS, NL, G, kPair>(warp - 3, lane, stg, lob, stg_full, stg_empty, lof, loe, acc_full,
+                                               acc_empty, abort_flag, a, tmem, n0, r_begin, r_end, nk, groups, tiles,
+                                               rank);
     } else if constexpr (kBits) {
       bits_converter<NS, G>(warp - 3, lane, stg, chk, stg_empty, acc_full, acc_empty, abort_flag, a, tmem, n0, r_begin,
                             r_end, nk, groups, tiles);
@@ -622,7 +700,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
     // one 64-wide K chunk of the weights: four 16 KB pieces -> TMEM buffer ja & 1
     auto load_chunk = [&]() -> bool {
       const int ab = ja & 1;
-      if (ja >= 2 && !mbar_wait(&a_empty[ab], ((ja >> 1) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT)) return false;
+      if (ja >= 2 && !mbar_wait<kPair>(&a_empty[ab], ((ja >> 1) - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))
+        return false;
       tc_fence_after();
       for (int p = 0; p < PPC; ++p, ++jp) {
         const int sp = jp % NP;
@@ -644,7 +723,10 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[ab]);
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_rank0(&a_full[ab]);  // the pair's MMAs wait on CTA 0's barrier
+        else mbar_arrive(&a_full[ab]);
+      }
       ++ja;
       return true;
     };
@@ -728,9 +810,11 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   }
 
   role_join();
+  if constexpr (kPair) cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still works
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, wt::kTmemCols);
+    if constexpr (kPair) tmem_dealloc_pair(tmem, wt::kTmemCols);
+    else tmem_dealloc(tmem, wt::kTmemCols);
   }
 }
 
@@ -740,19 +824,65 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
 // lo k0-31 | lo k32-63, each 128 rows x 128 B in the 128-byte swizzle, and in
 // the bf16 region (a.wimg_b16) the linear op's pieces bf16(w - hi) k0-63 |
 // bf16(hi) k0-63 of the same size.
-template <int kEpi, bool kRelu, bool kBits = false>
-int launch_wt_inst(const CUtensorMap& map, const TcArgs& a, int n_tiles, cudaStream_t stream) {
-  auto kern = spike_linear_wt_kernel<kEpi, kRelu, kBits>;
-  constexpr size_t smem = wt::Ring<kRelu, kEpi == kEpiGsmc>::kSmemBytes;
+template <int kEpi, bool kRelu, bool kBits = false, bool kPair = false>
+int launch_wt_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t stream) {
+  auto kern = spike_linear_wt_kernel<kEpi, kRelu, kBits, kPair>;
+  constexpr size_t smem = wt::Ring<kRelu, kEpi == kEpiGsmc, kPair>::kSmemBytes;
   SPK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int pairs_fit = 0;
+  if constexpr (kPair) {
+    // as many row ranges as keep every pair resident at once (pairs need two SMs of one
+    // cluster-capable group, so fewer than SMs / 2 may fit): no second wave
+    static int max_pairs[64];
+    int dev = 0;
+    SPK_CUDA_TRY(cudaGetDevice(&dev));
+    int& mp = max_pairs[dev & 63];
+    if (mp <= 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)n_tiles, 1);
+      cfg.blockDim = dim3(wt::kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      SPK_CUDA_TRY(cudaOccupancyMaxActiveClusters(&mp, kern, &cfg));
+      if (mp <= 0) return fail(SPK_ECUDA, "the CTA-pair kernel fits no cluster on this device");
+    }
+    pairs_fit = mp;
+    const int ranges = mp / (n_tiles / 2) > 0 ? mp / (n_tiles / 2) : 1;
+    a.rows_per_cta = ceil_div(ceil_div(a.R, ranges), 32) * 32;
+  }
   const int64_t gx = ceil_div(a.R, a.rows_per_cta);
-  dim3 grid((unsigned)gx, (unsigned)n_tiles);
+  const dim3 grid = kPair ? dim3((unsigned)n_tiles, (unsigned)gx) : dim3((unsigned)gx, (unsigned)n_tiles);
   prof_before(SPK_KERNEL_DENSE, stream);
-  SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(wt::kThreads), smem, stream, map, a));
+  if constexpr (kPair) {
+    const cudaError_t e = launch_dependent_cluster(kern, grid, dim3(wt::kThreads), smem, stream, 2u, true, map, a);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(SPK_ECUDA, "CTA-pair launch failed: %s (grid %u x %u, %zu B shared, %d pairs fit)",
+                  cudaGetErrorString(e), grid.x, grid.y, smem, pairs_fit);
+    }
+  } else {
+    SPK_CUDA_TRY(launch_dependent(kern, grid, dim3(wt::kThreads), smem, stream, map, a));
+  }
   prof_after(SPK_KERNEL_DENSE, stream);
   SPK_LAUNCH_CHECK();
   count_launch(1);
   return SPK_OK;
+}
+
+// CTA pairs for the linear op: SPK_WT_PAIR=1 in the environment turns them on
+// (read at every launch, so a test can compare both forms in one process).
+// Off by default: bit-identical to the single-CTA form but slower at the
+// model's geometries (the pair's MMAs wait for the slower CTA's converters and
+// for both CTAs' epilogues every group).
+inline bool wt_pair_enabled() {
+  const char* e = getenv("SPK_WT_PAIR");
+  return e != nullptr && atoi(e) != 0;
 }
 
 inline TcArgs wt_args(int64_t R, int K, int N, const TcPlan& p, const unsigned char* img, const TcOut& o, float thr) {
@@ -794,13 +924,25 @@ int launch_wt(const float* S, int64_t R, int K, int N, const TcPlan& p, const un
   int rc = make_map_2d_swizzled_f32(&map, S, R, K, K, 32, wt::kBoxRows, "S");
   if (rc) return rc;
   const TcArgs a = wt_args(R, K, N, p, img, o, thr);
+  // the linear op in CTA pairs when the N tiles pair up (no automatic-choice gate on this op)
+  const bool pair = act >= 0 && p.n_tiles % 2 == 0 && o.gate == nullptr && wt_pair_enabled();
   switch (act) {
     case -1: return launch_wt_inst<kEpiLinear, true>(map, a, p.n_tiles, stream);
-    case kEpiLinear: return launch_wt_inst<kEpiLinear, false>(map, a, p.n_tiles, stream);
-    case kEpiHeaviside: return launch_wt_inst<kEpiHeaviside, false>(map, a, p.n_tiles, stream);
-    case kEpiVSpike: return launch_wt_inst<kEpiVSpike, false>(map, a, p.n_tiles, stream);
-    case kEpiHeavisideBits: return launch_wt_inst<kEpiHeavisideBits, false>(map, a, p.n_tiles, stream);
-    case kEpiVSpikeBits: return launch_wt_inst<kEpiVSpikeBits, false>(map, a, p.n_tiles, stream);
+    case kEpiLinear:
+      return pair ? launch_wt_inst<kEpiLinear, false, false, true>(map, a, p.n_tiles, stream)
+                  : launch_wt_inst<kEpiLinear, false>(map, a, p.n_tiles, stream);
+    case kEpiHeaviside:
+      return pair ? launch_wt_inst<kEpiHeaviside, false, false, true>(map, a, p.n_tiles, stream)
+                  : launch_wt_inst<kEpiHeaviside, false>(map, a, p.n_tiles, stream);
+    case kEpiVSpike:
+      return pair ? launch_wt_inst<kEpiVSpike, false, false, true>(map, a, p.n_tiles, stream)
+                  : launch_wt_inst<kEpiVSpike, false>(map, a, p.n_tiles, stream);
+    case kEpiHeavisideBits:
+      return pair ? launch_wt_inst<kEpiHeavisideBits, false, false, true>(map, a, p.n_tiles, stream)
+                  : launch_wt_inst<kEpiHeavisideBits, false>(map, a, p.n_tiles, stream);
+    case kEpiVSpikeBits:
+      return pair ? launch_wt_inst<kEpiVSpikeBits, false, false, true>(map, a, p.n_tiles, stream)
+                  : launch_wt_inst<kEpiVSpikeBits, false>(map, a, p.n_tiles, stream);
     default: break;
   }
   return fail(SPK_EINVAL, "unknown activation %d", act);

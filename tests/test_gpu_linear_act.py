@@ -153,3 +153,25 @@ def test_packed_paths_with_no_rows():
     assert ops.linear_act(x, w, None, act="heaviside_bits").shape == (0, 4)
     bits = torch.empty(3, 0, 2, dtype=torch.int32, device="cuda")
     assert ops.spike_linear_bits(bits, 64, w).shape == (3, 0, 128)
+
+
+@pytest.mark.parametrize("R,K,N,act", [(1000, 512, 512, "none"), (257, 96, 256, "none"),
+                                       (4097, 64, 256, "heaviside_bits"), (3, 4, 256, "vspike"),
+                                       (65536, 512, 2048, "heaviside")])
+def test_cta_pair_form_is_bit_identical(R, K, N, act, monkeypatch):
+    """SPK_WT_PAIR=1 runs the linear op in CTA pairs (clusters of two CTAs
+    along N, tcgen05 cta_group::2 with M = 256: the two N tiles' weights in the
+    pair's TMEM, each CTA staging half of every 128-row tile): the same
+    products summed in the same order as the single-CTA form, so the output is
+    bit-identical, partial tiles and a rank whose half lies past the last row
+    included."""
+    g = torch.Generator(device="cuda").manual_seed(R + K + N)
+    x = torch.randn(R, K, generator=g, device="cuda")
+    w = torch.randn(N, K, generator=g, device="cuda") / K ** 0.5
+    b = torch.randn(N, generator=g, device="cuda") * 0.1
+    thr = 0.5 if act == "vspike" else 0.0
+    monkeypatch.setenv("SPK_WT_PAIR", "0")
+    single = ops.linear_act(x, w, b, act=act, thr=thr)
+    monkeypatch.setenv("SPK_WT_PAIR", "1")
+    pair = ops.linear_act(x, w, b, act=act, thr=thr)
+    assert torch.equal(single, pair)
