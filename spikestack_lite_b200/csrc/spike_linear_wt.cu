@@ -86,7 +86,7 @@ struct Ring {
   static constexpr size_t kRing =
       (size_t)(NS + NL) * Geo<kPair>::kStg + (size_t)kNP * kPieceBytes + kXchgBytes;
   // barriers, lo flags [NS][16] bytes, row counts [G][128], TMEM slot, abort flag
-  static constexpr int kBarsUsed = 5 * NS + 2 * NL + 2 * kNP + 7;
+  static constexpr int kBarsUsed = 5 * NS + 2 * NL + 2 * kNP + 8;
   static constexpr int kBars = kBarsUsed + (kBarsUsed & 1);  // even: the lo flags after them stay 16-byte aligned
   static constexpr size_t kTail = 8 * kBars + kConvWarps * NS + 4 * kRows * kG + 16;
   static constexpr size_t kSmemBytes = 1024 + kRing + ((kTail + 255) / 256) * 256;
@@ -187,7 +187,19 @@ __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int
   const int nb = (int)ceil_div(min64((int64_t)tg * wt::kRows, r_end - grow0), 16);
   const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + wt::kDcol;
   const int n = n0 + q * 32 + lane;
+  // tile by tile (blocks of tile t: 8t .. 8t + 7), each tile released on its own barrier as soon as
+  // it is drained, so the next group's MMAs into tile 0 start while tile 1 drains
+  bool released0 = false;
   for (int b = sq; b < nb; b += 4) {  // warp-uniform bounds
+    if (b >= 8 && !released0) {       // first block of tile 1 for this warp: its part of tile 0 is done
+      released0 = true;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_rank0(&acc_empty[0]);
+        else mbar_arrive(&acc_empty[0]);
+      }
+    }
     float v[16];
     tmem_ld16(tacc + (uint32_t)(16 * b), v);
     tmem_wait_ld();
@@ -218,9 +230,11 @@ __device__ __forceinline__ bool converter_group_epilogue(const int cw, const int
   }
   tc_fence_before();
   __syncwarp();
-  if (lane == 0) {
-    if constexpr (kPair) mbar_arrive_rank0(acc_empty);  // the pair's MMAs wait on CTA 0's barrier
-    else mbar_arrive(acc_empty);
+  if (lane == 0) {  // the tiles not released above (every warp releases both once per group)
+    for (int t = released0 ? 1 : 0; t < 2; ++t) {
+      if constexpr (kPair) mbar_arrive_rank0(&acc_empty[t]);  // the pair's MMAs wait on CTA 0's barriers
+      else mbar_arrive(&acc_empty[t]);
+    }
   }
   return true;
 }
@@ -410,11 +424,11 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
   uint64_t* a_full = pc_empty + NP;   // [2] weight chunk in TMEM
   uint64_t* a_empty = a_full + 2;     // [2]
   uint64_t* acc_full = a_empty + 2;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_empty + 1;
+  uint64_t* acc_empty = acc_full + 1;  // [2] row tile t of the accumulators drained
+  uint64_t* drain = acc_empty + 2;
   uint64_t* lof = drain + 1;   // [NL] correction buffer written (linear op)
   uint64_t* loe = lof + NL;    // [NL] correction buffer read by the MMAs
-  static_assert(5 * NS + 2 * NP + 7 + 2 * NL == RG::kBarsUsed, "the barriers above fill the barrier block");
+  static_assert(5 * NS + 2 * NP + 8 + 2 * NL == RG::kBarsUsed, "the barriers above fill the barrier block");
   uint8_t* lo_flag = reinterpret_cast<uint8_t*>(bars + RG::kBars);  // [NS][CW] bytes, 16-byte aligned
   int* row_count = reinterpret_cast<int*>(lo_flag + NS * CW);       // [G][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(row_count + G * wt::kRows);
@@ -449,7 +463,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       mbar_init(&a_empty[b], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, (kRelu && !kBits) ? 4 : CW * kCtas);  // the epilogue warps: loaders or converters
+    for (int t = 0; t < 2; ++t)  // the epilogue warps: loaders or converters
+      mbar_init(&acc_empty[t], (kRelu && !kBits) ? 4 : CW * kCtas);
     mbar_init(drain, 1);
     for (int l = 0; l < NL; ++l) {
       mbar_init(&lof[l], CW * kCtas);
@@ -549,9 +564,8 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       for (int g = 0; g < groups && ok; ++g) {
         const int pg = groups - 1 - g;  // groups in reverse order: the partial group first
     const int tg = min(G, tiles - pg * G);
-        // the accumulators are single-buffered: the previous group's epilogue has read them
-        if (g >= 1 && !(ok = mbar_wait<kPair>(acc_empty, (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
-        tc_fence_after();
+        // the accumulators are single-buffered: before its first MMA into row tile t the group
+        // waits until the previous group's epilogue has released that tile (below, at kc == 0)
         for (int kc = 0; kc < nk && ok; ++kc) {
           const int ab = ja & 1;
           if (!(ok = mbar_wait<kPair>(&a_full[ab], (ja >> 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
@@ -560,6 +574,10 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
           const uint32_t a_lo = a_hi + 64u;
           for (int t = 0; t < tg; ++t) {
             const int s = j % NS;
+            if (g >= 1 && kc == 0) {
+              if (!(ok = mbar_wait<kPair>(&acc_empty[t], (g - 1) & 1, abort_flag, SPK_DEV_PIPE_TIMEOUT))) break;
+              tc_fence_after();
+            }
             if constexpr (!kRelu) {
               // linear op: the tf32 pass w_hi * x_t (the slot as the tensor core reads it), then the
               // bf16 correction pass over K = 128: [bf16(w - w_hi) | bf16(w_hi)] (TMEM columns
@@ -804,7 +822,10 @@ __global__ void __launch_bounds__(wt::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[0]);
+        mbar_arrive(&acc_empty[1]);
+      }
     }
     tmem_wait_st();
   }
