@@ -412,7 +412,11 @@ constexpr int kRowsPerWarp = 32 / kLanesPerRow;
 constexpr int kWarpBuf = 1024;                              // column slots staged per warp
 constexpr size_t kMaskSmem = sizeof(int32_t) * kMaskWarps * kWarpBuf;
 
-__global__ void __launch_bounds__(kMaskThreads) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
+// Six CTAs per SM (at most 42 registers a thread, the largest shared-memory
+// carveout): 888 resident CTAs, so the 768 of the isolated config's 3 x 16384
+// rows run in one wave instead of five per SM plus a tail.
+constexpr int kMaskCtasPerSm = 6;
+__global__ void __launch_bounds__(kMaskThreads, kMaskCtasPerSm) csr_from_masks_kernel(CsrArgs a, int64_t tiles_pp) {
   if (gated_off(a.gate, a.gate_value)) return;
   extern __shared__ __align__(16) int32_t s_buf_all[];  // [kMaskWarps][kWarpBuf]
   __shared__ int64_t s_red[2 * kMaskWarps];
@@ -625,6 +629,8 @@ int launch_csr_scan_ex(const float* S, const uint32_t* bitmap, const int32_t* ro
     prof_before(SPK_KERNEL_CSR_SCAN, stream);
     SPK_CUDA_TRY(cudaFuncSetAttribute(csr_from_masks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kMaskSmem));
+    SPK_CUDA_TRY(cudaFuncSetAttribute(csr_from_masks_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      (int)cudaSharedmemCarveoutMaxShared));
     SPK_CUDA_TRY(launch_dependent(csr_from_masks_kernel, dim3((unsigned)(tpp * T)), dim3(kMaskThreads), kMaskSmem,
                                   stream, a, tpp));
     prof_after(SPK_KERNEL_CSR_SCAN, stream);
