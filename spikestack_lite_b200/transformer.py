@@ -38,7 +38,10 @@ class SpireEncoder(nn.Module):
         self.dither = nn.Parameter(torch.linspace(-0.05, 0.05, self.n_repeats).view(1, 1, 1, self.n_repeats))
 
     def forward(self, x):
-        u = self.projection(x)
+        # inference: the projection on the engine's tensor-core linear (as the blocks' projections)
+        u = ops.engine_linear(self.projection, x)
+        if u is None:
+            u = self.projection(x)
         if (self.temporal and not torch.is_grad_enabled() and u.is_cuda and u.dtype == torch.float32
                 and self.d_model % 4 == 0):
             # inference: the planes in one engine pass from u, (R, B, N, d)
