@@ -854,10 +854,10 @@ int launch_wt_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t s
   if constexpr (kPair) {
     // as many row ranges as keep every pair resident at once (pairs need two SMs of one
     // cluster-capable group, so fewer than SMs / 2 may fit): no second wave
-    static int max_pairs[64];
+    static std::atomic<int> max_pairs[64];  // per device; host threads may launch concurrently
     int dev = 0;
     SPK_CUDA_TRY(cudaGetDevice(&dev));
-    int& mp = max_pairs[dev & 63];
+    int mp = max_pairs[dev & 63].load(std::memory_order_relaxed);
     if (mp <= 0) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)n_tiles, 1);
@@ -872,6 +872,7 @@ int launch_wt_inst(const CUtensorMap& map, TcArgs a, int n_tiles, cudaStream_t s
       cfg.numAttrs = 1;
       SPK_CUDA_TRY(cudaOccupancyMaxActiveClusters(&mp, kern, &cfg));
       if (mp <= 0) return fail(SPK_ECUDA, "the CTA-pair kernel fits no cluster on this device");
+      max_pairs[dev & 63].store(mp, std::memory_order_relaxed);
     }
     pairs_fit = mp;
     const int ranges = mp / (n_tiles / 2) > 0 ? mp / (n_tiles / 2) : 1;

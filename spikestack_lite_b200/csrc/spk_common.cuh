@@ -14,6 +14,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/spikestack_b200.h"
